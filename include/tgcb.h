@@ -1,0 +1,138 @@
+/*
+ * tgcb: B200 (sm_100a) execution backend for tgc's compiled graphs. C-ABI of libtgcb.so.
+ *
+ * tgc runs a compiled graph as generated Python calling torch against one arena
+ * (tgc/runtime/executor.py:91-122, tgc/codegen/emit.py:165-209). This library is the seam
+ * that replaces the last two steps of compile_graph (emit + exec) and the call
+ * CompiledGraph.function(arena, inputs) (executor.py:52-88):
+ *
+ *   tgc step                                   | entry point here
+ *   -------------------------------------------+------------------------------------------
+ *   emit() writes source              emit.py:165 | host side writes CUDA source per plan
+ *   compile(source) + exec     executor.py:110-113 | tgcb_compile_cubin + tgcb_module_load
+ *   namespace["compiled"]         executor.py:113 | tgcb_plan_create
+ *   compiled(arena, inputs)        executor.py:79 | tgcb_plan_run
+ *
+ * plus the reduction and quantisation kernels tgc keeps outside the graph:
+ *   summation.sequential / pairwise (tgc/analysis/summation.py:56-85)
+ *                                           -> tgcb_sum_sequential_f32 / tgcb_sum_pairwise_f32
+ *   quantize.symmetric_scheme + quantise per row (tgc/analysis/quantize.py:90-128, 229-240)
+ *                                           -> tgcb_quantise_rows_i8
+ *
+ * Conventions: every function returns 0 on success or a negative TGCB_E_* status and never
+ * traps; tgcb_last_error() returns the calling thread's message for the last failure.
+ * Pointers are device pointers unless named host_*. Streams are cudaStream_t passed as
+ * void* (NULL = the legacy default stream). No torch types cross this boundary.
+ */
+#ifndef TGCB_H_
+#define TGCB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TGCB_OK 0
+#define TGCB_E_INVALID (-1)  /* bad argument: maps to ConfigError / AllocationError */
+#define TGCB_E_CUDA (-2)     /* CUDA runtime failure */
+#define TGCB_E_COMPILE (-3)  /* NVRTC rejected the generated source: maps to CodegenError */
+#define TGCB_E_DEVICE (-4)   /* a kernel reported a device-side timeout in the status word */
+#define TGCB_E_NOT_FOUND (-5)
+
+#define TGCB_MAX_INPUTS 48
+
+typedef struct tgcb_module tgcb_module;
+typedef struct tgcb_plan tgcb_plan;
+
+/* Where a GEMM operand lives and how TMA tiles it (row-major storage rows x cols). */
+typedef struct tgcb_operand_desc {
+  int32_t input_index;   /* >= 0: graph input slot; -1: arena */
+  uint32_t elem_bytes;   /* 4 (float32 read as tf32) or 1 (int8) */
+  uint64_t arena_offset; /* bytes from the arena base when input_index < 0 */
+  uint64_t rows;
+  uint64_t cols;
+  uint32_t box_cols;     /* TMA box extent along the contiguous axis (elements) */
+  uint32_t box_rows;     /* TMA box extent along rows */
+  uint32_t swizzle;      /* 0: 128-byte swizzle of 16-byte units; 1: of 32-byte units (tf32 MN-major) */
+  uint32_t reserved;
+} tgcb_operand_desc;
+
+/* One kernel launch of a plan. Plain kernels take TgcbArgs; GEMM kernels take TgcbArgs
+ * and two tensor maps that tgcb_plan_run encodes from a and b. */
+typedef struct tgcb_launch_desc {
+  char kernel[96];
+  uint32_t grid[3];
+  uint32_t block[3];
+  uint32_t smem_bytes;
+  uint32_t is_gemm;
+  tgcb_operand_desc a;
+  tgcb_operand_desc b;
+} tgcb_launch_desc;
+
+/* Library version string. */
+const char* tgcb_version(void);
+
+/* Message of the calling thread's last failure ("" if none). */
+const char* tgcb_last_error(void);
+
+/* Select `device`, allocate its status word and resolve the driver's tensor-map encoder.
+ * Idempotent per device. Replaces nothing in tgc (tgc is single-device CPU). */
+int tgcb_init(int device);
+
+/* Number of CUDA devices visible (0 on a host without a GPU). Never fails. */
+int tgcb_device_count(void);
+
+/* Compile CUDA C++ source for sm_100a with NVRTC (-std=c++17 --fmad=false, include_dir on
+ * the include path). On success *cubin is malloc'd (free with tgcb_free); on a compile
+ * error *log holds NVRTC's log (malloc'd) and TGCB_E_COMPILE is returned.
+ * Replaces: compile(module.source, "<tgc>", "exec") (tgc/runtime/executor.py:112). */
+int tgcb_compile_cubin(const char* source, const char* include_dir, const char* const* extra_options,
+                       int n_extra_options, void** cubin, size_t* cubin_size, char** log);
+
+void tgcb_free(void* p);
+
+/* Load a cubin produced by tgcb_compile_cubin into the current context. */
+int tgcb_module_load(const void* cubin, size_t size, tgcb_module** out);
+void tgcb_module_unload(tgcb_module* m);
+
+/* Resolve each launch's kernel in `m` and keep the descriptors.
+ * Replaces: namespace["compiled"] (tgc/runtime/executor.py:113). */
+int tgcb_plan_create(tgcb_module* m, const tgcb_launch_desc* launches, int n_launches, uint64_t arena_bytes,
+                     tgcb_plan** out);
+void tgcb_plan_destroy(tgcb_plan* p);
+
+/* Launch every kernel of the plan in order on `stream`. `arena` is a device allocation of at
+ * least arena_bytes (256-byte aligned); inputs[i] is the device address of graph input i
+ * (read only). Asynchronous: returns after the launches are queued.
+ * Replaces: compiled(arena, inputs) (tgc/runtime/executor.py:79, generated by emit.py:165-209). */
+int tgcb_plan_run(tgcb_plan* p, void* arena, const void* const* inputs, int n_inputs, void* stream);
+
+/* Number of launches a plan queues per run. */
+int tgcb_plan_launch_count(const tgcb_plan* p);
+
+/* Read (and with clear != 0, reset) the device status word of the current device.
+ * Synchronises the device. *status = 0 means every kernel so far completed normally. */
+int tgcb_status(int clear, int* status);
+
+/* Pairwise sum, block 8, bit-exact to tgc/analysis/summation.py:64-85 (_pairwise): halve the
+ * range at size//2 until it is <= block, sum blocks sequentially from 0.0f, add halves.
+ * `scratch` must hold tgcb_sum_pairwise_scratch_bytes(n, block) bytes. Writes *out (device). */
+size_t tgcb_sum_pairwise_scratch_bytes(uint64_t n, int block);
+int tgcb_sum_pairwise_f32(const float* x, uint64_t n, int block, float* out, void* scratch, size_t scratch_bytes,
+                          void* stream);
+
+/* Sequential sum from 0.0f left to right, bit-exact to tgc/analysis/summation.py:56-61. */
+int tgcb_sum_sequential_f32(const float* x, uint64_t n, float* out, void* stream);
+
+/* Per-row symmetric int8 quantisation, bit-exact to quantize.symmetric_scheme + quantise
+ * applied per row (tgc/analysis/quantize.py:90-128, 229-240): m = max|row| in float32,
+ * scale = float((double)m / 127) (1.0f for an all-zero row), q = rint(x / scale) clamped to
+ * [-128, 127]. Writes q[rows*cols] (int8) and scale[rows] (float32). */
+int tgcb_quantise_rows_i8(const float* x, int64_t rows, int64_t cols, int8_t* q, float* scale, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TGCB_H_ */

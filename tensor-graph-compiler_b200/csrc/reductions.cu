@@ -1,0 +1,284 @@
+// Long reductions and the per-row int8 quantiser, compiled ahead of time into libtgcb.so.
+//
+// Pairwise sum (tgc/analysis/summation.py:64-85). tgc's _pairwise halves a range at
+// size//2 until it holds at most `block` values, sums each block sequentially from 0.0f and
+// adds the two halves. With L the deepest level at which every node is still larger than
+// `block` plus one, the top L levels are a perfect binary tree over 2^L nodes in index order,
+// and every depth-L node needs at most one more split. So:
+//   * level 0: thread j computes depth-L node j (a closed form start = j * (n >> L) when 2^L
+//     divides n, otherwise a walk of the L halvings), sums it exactly like _pairwise, and
+//     256-node groups are combined as perfect trees in shared memory;
+//   * levels 1..: the same perfect-tree combine over 256 partials at a time, until one.
+// Every addition is the one _pairwise performs, so the result is bit-identical.
+//
+// Sequential sum (summation.py:56-61) is one dependent chain of n float additions; one
+// thread runs it with the loads software-pipelined ahead of the chain.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "tgcb.h"
+
+// Records the calling thread's last error (defined in runtime.cu).
+int tgcb_internal_fail(int code, const char* what, const char* detail);
+
+namespace {
+
+int report(int code, const char* what, cudaError_t e) { return tgcb_internal_fail(code, what, cudaGetErrorString(e)); }
+
+constexpr int kGroup = 256;
+
+__device__ __forceinline__ float seq_sum(const float* __restrict__ x, long long start, long long size) {
+  float t = 0.0f;
+  for (long long i = 0; i < size; ++i) t = __fadd_rn(t, __ldg(x + start + i));
+  return t;
+}
+
+// Value of the depth-L node [start, start+size) under _pairwise's rules (size <= 2*block+1).
+__device__ __forceinline__ float node_value(const float* __restrict__ x, long long start, long long size, int block) {
+  if (size <= block) return seq_sum(x, start, size);
+  const long long h = size / 2;
+  return __fadd_rn(seq_sum(x, start, h), seq_sum(x, start + h, size - h));
+}
+
+// Perfect-tree combine of `count` (power of two, <= 256) values held in s[0..count).
+__device__ __forceinline__ float tree256(float* s, int count) {
+  for (int w = 1; w < count; w *= 2) {
+    __syncthreads();
+    const int t = threadIdx.x;
+    if ((t % (2 * w)) == 0 && t + w < count) s[t] = __fadd_rn(s[t], s[t + w]);
+  }
+  __syncthreads();
+  return s[0];
+}
+
+__global__ void __launch_bounds__(kGroup) pairwise_leaves(const float* __restrict__ x, long long n, int L, int block,
+                                                          int uniform, float* __restrict__ out) {
+  __shared__ float s[kGroup];
+  const long long nodes = 1ll << L;
+  const long long j = (long long)blockIdx.x * kGroup + threadIdx.x;
+  float v = 0.0f;
+  if (j < nodes) {
+    long long start, size;
+    if (uniform) {
+      size = n >> L;
+      start = j * size;
+    } else {
+      start = 0;
+      size = n;
+      for (int lvl = L - 1; lvl >= 0; --lvl) {
+        const long long half = size / 2;
+        if ((j >> lvl) & 1) {
+          start += half;
+          size -= half;
+        } else {
+          size = half;
+        }
+      }
+    }
+    if (uniform && size == 8 && block >= 8 && ((reinterpret_cast<uintptr_t>(x + start) & 15u) == 0)) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(x + start));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(x + start) + 1);
+      float t = 0.0f;
+      t = __fadd_rn(t, a.x);
+      t = __fadd_rn(t, a.y);
+      t = __fadd_rn(t, a.z);
+      t = __fadd_rn(t, a.w);
+      t = __fadd_rn(t, b.x);
+      t = __fadd_rn(t, b.y);
+      t = __fadd_rn(t, b.z);
+      t = __fadd_rn(t, b.w);
+      v = t;
+    } else {
+      v = node_value(x, start, size, block);
+    }
+  }
+  s[threadIdx.x] = v;
+  const int count = (int)(nodes < kGroup ? nodes : kGroup);
+  const float r = tree256(s, count);
+  if (threadIdx.x == 0) out[blockIdx.x] = r;
+}
+
+__global__ void __launch_bounds__(kGroup) pairwise_combine(const float* __restrict__ in, long long count,
+                                                           float* __restrict__ out) {
+  __shared__ float s[kGroup];
+  const long long j = (long long)blockIdx.x * kGroup + threadIdx.x;
+  s[threadIdx.x] = j < count ? in[j] : 0.0f;
+  const int c = (int)(count < kGroup ? count : kGroup);
+  const float r = tree256(s, c);
+  if (threadIdx.x == 0) out[blockIdx.x] = r;
+}
+
+__global__ void sequential_chain(const float* __restrict__ x, long long n, float* __restrict__ out) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  float t = 0.0f;
+  long long i = 0;
+  const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+  if (aligned) {
+    const float4* v = reinterpret_cast<const float4*>(x);
+    const long long nv = n / 4;
+    constexpr int D = 16;  // float4 loads kept in flight ahead of the chain
+    float4 buf[D];
+    long long q = 0;
+#pragma unroll
+    for (int k = 0; k < D; ++k) buf[k] = (q + k < nv) ? __ldg(v + q + k) : make_float4(0, 0, 0, 0);
+    for (; q + D <= nv; q += D) {
+#pragma unroll
+      for (int k = 0; k < D; ++k) {
+        const float4 c = buf[k];
+        if (q + D + k < nv) buf[k] = __ldg(v + q + D + k);
+        t = __fadd_rn(t, c.x);
+        t = __fadd_rn(t, c.y);
+        t = __fadd_rn(t, c.z);
+        t = __fadd_rn(t, c.w);
+      }
+    }
+    for (long long k = 0; q + k < nv; ++k) {
+      const float4 c = buf[k];
+      t = __fadd_rn(t, c.x);
+      t = __fadd_rn(t, c.y);
+      t = __fadd_rn(t, c.z);
+      t = __fadd_rn(t, c.w);
+    }
+    i = nv * 4;
+  }
+  for (; i < n; ++i) t = __fadd_rn(t, __ldg(x + i));
+  *out = t;
+}
+
+// One CTA per row. The row stays in registers between the max pass and the quantise pass.
+template <int PER_THREAD>
+__global__ void __launch_bounds__(256) quantise_rows(const float* __restrict__ x, long long rows, long long cols,
+                                                     int8_t* __restrict__ q, float* __restrict__ scale) {
+  __shared__ float red[8];
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* row = x + r * cols;
+    float v[PER_THREAD];
+    float m = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER_THREAD; ++k) {
+      const long long c = threadIdx.x + (long long)k * 256;
+      v[k] = c < cols ? __ldg(row + c) : 0.0f;
+      const float a = fabsf(v[k]);
+      m = (a > m || a != a) ? a : m;
+    }
+    for (long long c = threadIdx.x + (long long)PER_THREAD * 256; c < cols; c += 256) {
+      const float a = fabsf(__ldg(row + c));
+      m = (a > m || a != a) ? a : m;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float other = __shfl_xor_sync(0xffffffffu, m, o);
+      m = (other > m || other != other) ? other : m;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    float mm = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) mm = (red[w] > mm || red[w] != red[w]) ? red[w] : mm;
+    __syncthreads();
+    // scale = largest / 127 computed in double and read back as float32; 1.0 for a zero row.
+    const float s = (mm == 0.0f) ? 1.0f : (float)((double)mm / 127.0);
+    if (threadIdx.x == 0) scale[r] = s;
+    int8_t* qrow = q + r * cols;
+#pragma unroll
+    for (int k = 0; k < PER_THREAD; ++k) {
+      const long long c = threadIdx.x + (long long)k * 256;
+      if (c < cols) {
+        float t = rintf(__fdiv_rn(v[k], s));
+        t = fminf(fmaxf(t, -128.0f), 127.0f);
+        qrow[c] = (int8_t)(int)t;
+      }
+    }
+    for (long long c = threadIdx.x + (long long)PER_THREAD * 256; c < cols; c += 256) {
+      float t = rintf(__fdiv_rn(__ldg(row + c), s));
+      t = fminf(fmaxf(t, -128.0f), 127.0f);
+      qrow[c] = (int8_t)(int)t;
+    }
+  }
+}
+
+int levels_for(uint64_t n, int block) {
+  // deepest L with floor(n / 2^(L-1)) > block, i.e. every node above depth L is internal
+  int L = 0;
+  while ((n >> L) > (uint64_t)block) ++L;
+  return L;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t tgcb_sum_pairwise_scratch_bytes(uint64_t n, int block) {
+  if (n == 0 || block < 1) return 0;
+  const int L = levels_for(n, block);
+  uint64_t count = 1ull << L;
+  size_t total = 0;
+  while (true) {
+    const uint64_t groups = (count + kGroup - 1) / kGroup;
+    total += groups * sizeof(float);
+    if (groups <= 1) break;
+    count = groups;
+  }
+  return (total + 255) & ~size_t(255);
+}
+
+int tgcb_sum_pairwise_f32(const float* x, uint64_t n, int block, float* out, void* scratch, size_t scratch_bytes,
+                          void* stream) {
+  if (x == nullptr || out == nullptr) return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_pairwise_f32", "null pointer");
+  if (n == 0) return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_pairwise_f32", "there is nothing to sum");
+  if (block < 1) return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_pairwise_f32", "a block must hold at least one value");
+  const size_t need = tgcb_sum_pairwise_scratch_bytes(n, block);
+  if (scratch == nullptr || scratch_bytes < need)
+    return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_pairwise_f32", "scratch is smaller than tgcb_sum_pairwise_scratch_bytes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int L = levels_for(n, block);
+  const long long nodes = 1ll << L;
+  const int uniform = (n % (uint64_t)nodes) == 0 ? 1 : 0;
+  float* buf = static_cast<float*>(scratch);
+  long long groups = (nodes + kGroup - 1) / kGroup;
+  float* dst = groups == 1 ? out : buf;
+  pairwise_leaves<<<(unsigned)groups, kGroup, 0, s>>>(x, (long long)n, L, block, uniform, dst);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return report(TGCB_E_CUDA, "pairwise_leaves", e);
+  float* src = buf;
+  float* next = buf + groups;
+  while (groups > 1) {
+    const long long g2 = (groups + kGroup - 1) / kGroup;
+    float* d = g2 == 1 ? out : next;
+    pairwise_combine<<<(unsigned)g2, kGroup, 0, s>>>(src, groups, d);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return report(TGCB_E_CUDA, "pairwise_combine", e);
+    src = next;
+    next = next + g2;
+    groups = g2;
+  }
+  return TGCB_OK;
+}
+
+int tgcb_sum_sequential_f32(const float* x, uint64_t n, float* out, void* stream) {
+  if (x == nullptr || out == nullptr) return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_sequential_f32", "null pointer");
+  if (n == 0) return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_sequential_f32", "there is nothing to sum");
+  sequential_chain<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(x, (long long)n, out);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return report(TGCB_E_CUDA, "sequential_chain", e);
+  return TGCB_OK;
+}
+
+int tgcb_quantise_rows_i8(const float* x, int64_t rows, int64_t cols, int8_t* q, float* scale, void* stream) {
+  if (x == nullptr || q == nullptr || scale == nullptr)
+    return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_quantise_rows_i8", "null pointer");
+  if (rows < 1 || cols < 1) return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_quantise_rows_i8", "there is nothing to quantise");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned grid = (unsigned)(rows < 148 * 8 ? rows : 148 * 8);
+  if (cols <= 256 * 4)
+    quantise_rows<4><<<grid, 256, 0, s>>>(x, rows, cols, q, scale);
+  else
+    quantise_rows<16><<<grid, 256, 0, s>>>(x, rows, cols, q, scale);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return report(TGCB_E_CUDA, "quantise_rows", e);
+  return TGCB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,318 @@
+// libtgcb runtime: NVRTC compilation, module loading and plan execution.
+//
+// The library links the CUDA runtime statically and reaches the driver only through
+// cudaGetDriverEntryPoint, so it loads on a host without a GPU (the CPU test suite checks
+// its exports) and needs no libcuda at link time.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <nvrtc.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "tgcb.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[2048];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define CUDA_TRY(expr)                                                                               \
+  do {                                                                                               \
+    cudaError_t e_ = (expr);                                                                         \
+    if (e_ != cudaSuccess) return fail(TGCB_E_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e_)); \
+  } while (0)
+
+// Must match struct TgcbArgs in csrc/jit_common.cuh.
+struct TgcbArgs {
+  char* arena;
+  const char* in[TGCB_MAX_INPUTS];
+  int* status;
+};
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+constexpr int kMaxDevices = 16;
+struct DeviceState {
+  bool ready = false;
+  int* status = nullptr;
+  EncodeTiledFn encode = nullptr;
+};
+DeviceState g_devices[kMaxDevices];
+std::mutex g_mutex;
+
+int current_state(DeviceState** out) {
+  int dev = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(TGCB_E_INVALID, "device %d out of range", dev);
+  if (!g_devices[dev].ready) {
+    int rc = tgcb_init(dev);
+    if (rc != TGCB_OK) return rc;
+  }
+  *out = &g_devices[dev];
+  return TGCB_OK;
+}
+
+}  // namespace
+
+int tgcb_internal_fail(int code, const char* what, const char* detail) { return fail(code, "%s: %s", what, detail); }
+
+struct tgcb_module {
+  cudaLibrary_t lib = nullptr;
+};
+
+struct LaunchState {
+  tgcb_launch_desc desc;
+  cudaKernel_t kernel = nullptr;
+  const void* a_ptr = nullptr;
+  const void* b_ptr = nullptr;
+  alignas(64) CUtensorMap ta;
+  alignas(64) CUtensorMap tb;
+};
+
+struct tgcb_plan {
+  std::vector<LaunchState> launches;
+  uint64_t arena_bytes = 0;
+};
+
+extern "C" {
+
+const char* tgcb_version(void) { return "tgcb 0.1 (sm_100a)"; }
+
+const char* tgcb_last_error(void) { return g_last_error.c_str(); }
+
+void tgcb_free(void* p) { free(p); }
+
+int tgcb_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+int tgcb_init(int device) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (device < 0 || device >= kMaxDevices) return fail(TGCB_E_INVALID, "device %d out of range", device);
+  CUDA_TRY(cudaSetDevice(device));
+  DeviceState& st = g_devices[device];
+  if (st.ready) return TGCB_OK;
+  CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&st.status), 256));
+  CUDA_TRY(cudaMemset(st.status, 0, 256));
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  CUDA_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+  if (fn == nullptr || q != cudaDriverEntryPointSuccess)
+    return fail(TGCB_E_CUDA, "the driver does not provide cuTensorMapEncodeTiled");
+  st.encode = reinterpret_cast<EncodeTiledFn>(fn);
+  st.ready = true;
+  return TGCB_OK;
+}
+
+int tgcb_compile_cubin(const char* source, const char* include_dir, const char* const* extra_options,
+                       int n_extra_options, void** cubin, size_t* cubin_size, char** log) {
+  if (source == nullptr || cubin == nullptr || cubin_size == nullptr)
+    return fail(TGCB_E_INVALID, "tgcb_compile_cubin: null argument");
+  *cubin = nullptr;
+  *cubin_size = 0;
+  if (log) *log = nullptr;
+  nvrtcProgram prog;
+  nvrtcResult r = nvrtcCreateProgram(&prog, source, "tgcb_generated.cu", 0, nullptr, nullptr);
+  if (r != NVRTC_SUCCESS) return fail(TGCB_E_COMPILE, "nvrtcCreateProgram: %s", nvrtcGetErrorString(r));
+  std::vector<std::string> opts = {"--gpu-architecture=sm_100a", "-std=c++17", "--fmad=false", "-default-device",
+                                   "-lineinfo"};
+  if (include_dir) opts.push_back(std::string("-I") + include_dir);
+  for (int i = 0; i < n_extra_options; ++i) opts.push_back(extra_options[i]);
+  std::vector<const char*> copts;
+  for (auto& o : opts) copts.push_back(o.c_str());
+  r = nvrtcCompileProgram(prog, (int)copts.size(), copts.data());
+  size_t log_size = 0;
+  nvrtcGetProgramLogSize(prog, &log_size);
+  if (log && log_size > 1) {
+    *log = static_cast<char*>(malloc(log_size));
+    nvrtcGetProgramLog(prog, *log);
+  }
+  if (r != NVRTC_SUCCESS) {
+    nvrtcDestroyProgram(&prog);
+    return fail(TGCB_E_COMPILE, "NVRTC could not compile the generated source: %s", nvrtcGetErrorString(r));
+  }
+  size_t n = 0;
+  r = nvrtcGetCUBINSize(prog, &n);
+  if (r != NVRTC_SUCCESS || n == 0) {
+    nvrtcDestroyProgram(&prog);
+    return fail(TGCB_E_COMPILE, "nvrtcGetCUBINSize: %s", nvrtcGetErrorString(r));
+  }
+  void* buf = malloc(n);
+  r = nvrtcGetCUBIN(prog, static_cast<char*>(buf));
+  nvrtcDestroyProgram(&prog);
+  if (r != NVRTC_SUCCESS) {
+    free(buf);
+    return fail(TGCB_E_COMPILE, "nvrtcGetCUBIN: %s", nvrtcGetErrorString(r));
+  }
+  *cubin = buf;
+  *cubin_size = n;
+  return TGCB_OK;
+}
+
+int tgcb_module_load(const void* cubin, size_t size, tgcb_module** out) {
+  if (cubin == nullptr || size == 0 || out == nullptr) return fail(TGCB_E_INVALID, "tgcb_module_load: empty image");
+  DeviceState* st = nullptr;
+  int rc = current_state(&st);
+  if (rc != TGCB_OK) return rc;
+  auto* m = new tgcb_module();
+  cudaError_t e = cudaLibraryLoadData(&m->lib, cubin, nullptr, nullptr, 0, nullptr, nullptr, 0);
+  if (e != cudaSuccess) {
+    delete m;
+    return fail(TGCB_E_CUDA, "cudaLibraryLoadData: %s", cudaGetErrorString(e));
+  }
+  *out = m;
+  return TGCB_OK;
+}
+
+void tgcb_module_unload(tgcb_module* m) {
+  if (m == nullptr) return;
+  if (m->lib) cudaLibraryUnload(m->lib);
+  delete m;
+}
+
+int tgcb_plan_create(tgcb_module* m, const tgcb_launch_desc* launches, int n_launches, uint64_t arena_bytes,
+                     tgcb_plan** out) {
+  if (m == nullptr || out == nullptr || n_launches < 0 || (n_launches > 0 && launches == nullptr))
+    return fail(TGCB_E_INVALID, "tgcb_plan_create: bad arguments");
+  auto* p = new tgcb_plan();
+  p->arena_bytes = arena_bytes;
+  p->launches.resize(n_launches);
+  for (int i = 0; i < n_launches; ++i) {
+    LaunchState& ls = p->launches[i];
+    ls.desc = launches[i];
+    ls.desc.kernel[sizeof(ls.desc.kernel) - 1] = '\0';
+    cudaError_t e = cudaLibraryGetKernel(&ls.kernel, m->lib, ls.desc.kernel);
+    if (e != cudaSuccess) {
+      delete p;
+      return fail(TGCB_E_NOT_FOUND, "kernel %s not in module: %s", launches[i].kernel, cudaGetErrorString(e));
+    }
+    if (ls.desc.smem_bytes > 48 * 1024) {
+      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(ls.kernel), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)ls.desc.smem_bytes);
+      if (e != cudaSuccess) {
+        delete p;
+        return fail(TGCB_E_CUDA, "setting %u bytes of shared memory on %s: %s", ls.desc.smem_bytes, ls.desc.kernel,
+                    cudaGetErrorString(e));
+      }
+    }
+    for (const tgcb_operand_desc* od : {&ls.desc.a, &ls.desc.b}) {
+      if (!ls.desc.is_gemm) break;
+      if (od->input_index >= TGCB_MAX_INPUTS || (od->input_index < 0 && od->arena_offset + od->rows * od->cols *
+                                                                                                 od->elem_bytes >
+                                                                             arena_bytes)) {
+        delete p;
+        return fail(TGCB_E_INVALID, "operand of %s lies outside the arena or the input table", ls.desc.kernel);
+      }
+    }
+  }
+  *out = p;
+  return TGCB_OK;
+}
+
+void tgcb_plan_destroy(tgcb_plan* p) { delete p; }
+
+int tgcb_plan_launch_count(const tgcb_plan* p) { return p ? (int)p->launches.size() : 0; }
+
+static int encode_operand(DeviceState* st, const tgcb_operand_desc& od, const void* base, CUtensorMap* map) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return fail(TGCB_E_INVALID, "GEMM operand at %p is not 16-byte aligned", base);
+  if ((od.cols * od.elem_bytes) % 16 != 0)
+    return fail(TGCB_E_INVALID, "GEMM operand row pitch %llu bytes is not a multiple of 16",
+                (unsigned long long)(od.cols * od.elem_bytes));
+  cuuint64_t dims[2] = {od.cols, od.rows};
+  cuuint64_t strides[1] = {od.cols * od.elem_bytes};
+  cuuint32_t box[2] = {od.box_cols, od.box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUtensorMapDataType dt = od.elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapSwizzle sw = od.swizzle == 1 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+  CUresult r = st->encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TGCB_E_CUDA, "cuTensorMapEncodeTiled failed with %d", (int)r);
+  return TGCB_OK;
+}
+
+int tgcb_plan_run(tgcb_plan* p, void* arena, const void* const* inputs, int n_inputs, void* stream) {
+  if (p == nullptr) return fail(TGCB_E_INVALID, "tgcb_plan_run: null plan");
+  if (n_inputs < 0 || n_inputs > TGCB_MAX_INPUTS)
+    return fail(TGCB_E_INVALID, "a plan takes at most %d inputs, got %d", TGCB_MAX_INPUTS, n_inputs);
+  if (p->arena_bytes > 0 && arena == nullptr) return fail(TGCB_E_INVALID, "tgcb_plan_run: null arena");
+  if ((reinterpret_cast<uintptr_t>(arena) & 255u) != 0) return fail(TGCB_E_INVALID, "the arena is not 256-byte aligned");
+  DeviceState* st = nullptr;
+  int rc = current_state(&st);
+  if (rc != TGCB_OK) return rc;
+  TgcbArgs args;
+  memset(&args, 0, sizeof(args));
+  args.arena = static_cast<char*>(arena);
+  for (int i = 0; i < n_inputs; ++i) args.in[i] = static_cast<const char*>(inputs[i]);
+  args.status = st->status;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (LaunchState& ls : p->launches) {
+    const tgcb_launch_desc& d = ls.desc;
+    dim3 grid(d.grid[0], d.grid[1], d.grid[2]);
+    dim3 block(d.block[0], d.block[1], d.block[2]);
+    cudaError_t e;
+    if (d.is_gemm) {
+      const tgcb_operand_desc* ods[2] = {&d.a, &d.b};
+      const void** cached[2] = {&ls.a_ptr, &ls.b_ptr};
+      CUtensorMap* maps[2] = {&ls.ta, &ls.tb};
+      for (int k = 0; k < 2; ++k) {
+        const tgcb_operand_desc& od = *ods[k];
+        const void* base;
+        if (od.input_index >= 0) {
+          if (od.input_index >= n_inputs) return fail(TGCB_E_INVALID, "GEMM operand reads missing input %d", od.input_index);
+          base = inputs[od.input_index];
+        } else {
+          base = static_cast<const char*>(arena) + od.arena_offset;
+        }
+        if (base != *cached[k]) {
+          rc = encode_operand(st, od, base, maps[k]);
+          if (rc != TGCB_OK) return rc;
+          *cached[k] = base;
+        }
+      }
+      void* params[3] = {&args, &ls.ta, &ls.tb};
+      e = cudaLaunchKernel(reinterpret_cast<const void*>(ls.kernel), grid, block, params, d.smem_bytes, s);
+    } else {
+      void* params[1] = {&args};
+      e = cudaLaunchKernel(reinterpret_cast<const void*>(ls.kernel), grid, block, params, d.smem_bytes, s);
+    }
+    if (e != cudaSuccess) return fail(TGCB_E_CUDA, "launching %s: %s", d.kernel, cudaGetErrorString(e));
+  }
+  return TGCB_OK;
+}
+
+int tgcb_status(int clear, int* status) {
+  if (status == nullptr) return fail(TGCB_E_INVALID, "tgcb_status: null output");
+  DeviceState* st = nullptr;
+  int rc = current_state(&st);
+  if (rc != TGCB_OK) return rc;
+  CUDA_TRY(cudaDeviceSynchronize());
+  CUDA_TRY(cudaMemcpy(status, st->status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (clear) CUDA_TRY(cudaMemset(st->status, 0, sizeof(int)));
+  return TGCB_OK;
+}
+
+}  // extern "C"

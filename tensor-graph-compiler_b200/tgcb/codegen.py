@@ -1,0 +1,925 @@
+"""Lowering a scheduled graph to B200 kernel steps.
+
+This replaces tgc/codegen/emit.py:165-209. Where tgc writes one torch statement per node
+into arena views, this module partitions the graph into kernels and writes each kernel's
+CUDA source, which ``tgcb.runtime`` compiles with NVRTC for sm_100a and launches from the
+C library.
+
+Partitioning (the grouping tgc's passes/fusion.py and schedule/fusion_search.py reason
+about, made executable):
+
+* *Hard* values are graph inputs, ``matmul`` outputs and reduction outputs. Everything else
+  (elementwise ops, views, constants) is *soft*: it is recomputed inside whichever kernel
+  reads it and never touches HBM unless something forces it to.
+* Each ``matmul`` is one GEMM step (tcgen05 TF32 for float32, tcgen05 INT8 with an int32
+  accumulator when both operands are int8 values cast to int32). ``transpose`` and the
+  int8->int32 ``cast`` on an operand are absorbed into the operand's major-ness and type.
+* Reductions over the last axis that share a row space form one *row* step: a multi-phase
+  kernel that keeps one row per CTA, computes every reduction of a phase in one pass over
+  the row, and feeds them to the next phase (softmax, layernorm, the three-reduction cone).
+  Reductions over axis 0 of a matrix are *column* steps, over all axes *full* steps; other
+  axis sets fall back to a one-thread-per-output sequential kernel.
+* A soft value that must exist in memory (a graph output, or a GEMM operand) is a
+  *request*. It is written by the kernel that produces its latest hard dependency if it can
+  be computed there: a GEMM epilogue (bias, GELU, loss gradients), or a row step's final
+  phase (the normalised layernorm output). Otherwise it gets a standalone elementwise
+  *map* step right after its dependencies.
+* A hard value read by any kernel other than its producer is stored by its producer.
+
+Reductions declare their bracketing (the order additions happen in) and ``oracle/`` holds
+a CPU restatement of each one so reduction results can be checked bit-for-bit when the
+summands are exact; against tgc's interpreter (whose ATen order is unspecified) they are
+checked within a tolerance.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+from tgcb import ir
+from tgcb.errors import CodegenError
+from tgcb.expr import ExprBuilder, _broadcast_index, ctype, delinearise
+
+NUM_SMS = 148
+
+# Placeholder for the base pointer of a materialised value; replaced once the plan exists.
+def PTR(name: str) -> str:
+    return f"@P<{name}>@"
+
+
+@dataclass
+class GemmOperand:
+    value: str  # materialised 2-D value, row-major storage
+    rows: int  # storage rows
+    cols: int  # storage cols
+    mn_major: bool  # True when the M (or N) index runs along the contiguous storage axis
+    elem_bytes: int
+
+
+@dataclass
+class Launch:
+    kernel: str
+    grid: tuple[int, int, int]
+    block: tuple[int, int, int]
+    smem: int = 0
+    gemm: tuple[GemmOperand, GemmOperand] | None = None
+
+
+@dataclass
+class Step:
+    kind: str
+    label: str
+    reads: list[str] = field(default_factory=list)
+    writes: list[str] = field(default_factory=list)
+    source: str = ""
+    launches: list[Launch] = field(default_factory=list)
+    bracketing: str = ""
+    nodes: list[str] = field(default_factory=list)
+
+
+@dataclass
+class RowGroup:
+    members: list[str]
+    src_sizes: tuple[int, ...]
+    phase: dict[str, int] = field(default_factory=dict)
+
+
+def _prod(xs) -> int:
+    p = 1
+    for x in xs:
+        p *= x
+    return p
+
+
+def _next_pow2(x: int) -> int:
+    return 1 << max(0, (x - 1).bit_length())
+
+
+def row_threads(cols: int) -> int:
+    """Threads per row in a row kernel: a power of two in [32, 256], about 4 columns each."""
+    return max(32, min(256, _next_pow2(max(1, (cols + 3) // 4))))
+
+
+class Lowering:
+    """Partition ``graph`` (already optimised, nodes in ``order``) into kernel steps."""
+
+    def __init__(self, graph, order):
+        self.graph = graph
+        self.order = list(order)
+        self.values = {v.name: v for v in graph.inputs}
+        self.values.update({n.name: n.output for n in graph.nodes})
+        self.producers = {n.name: n for n in graph.nodes}
+        self.inputs = [v.name for v in graph.inputs]
+        self.outputs = list(graph.outputs)
+        for name, v in self.values.items():
+            if not v.shape.is_static:
+                raise CodegenError("a symbolic shape cannot be given a fixed offset in an arena")
+            ctype(v.dtype)
+        self._deps: dict[str, frozenset[str]] = {}
+        self.materialised: set[str] = set()  # hard values some other kernel reads
+        self.requests: dict[str, str] = {}  # soft value -> owner key
+        self.steps: list[Step] = []
+        self.scratch: dict[str, int] = {}  # scratch slot name -> bytes
+        self.kernel_count = 0
+
+    # ------------------------------------------------------------------ classification
+
+    def is_hard(self, name: str) -> bool:
+        node = self.producers.get(name)
+        if node is None:
+            return True
+        return node.op.category in (ir.REDUCTION, ir.CONTRACTION)
+
+    def hard_deps(self, name: str) -> frozenset[str]:
+        """Hard values reachable from ``name`` through soft nodes (itself if hard)."""
+        if name in self._deps:
+            return self._deps[name]
+        if self.is_hard(name):
+            out = frozenset([name])
+        else:
+            acc: set[str] = set()
+            for i in self.producers[name].inputs:
+                acc |= self.hard_deps(i)
+            out = frozenset(acc)
+        self._deps[name] = out
+        return out
+
+    def sizes(self, name: str) -> tuple[int, ...]:
+        return self.values[name].shape.ints()
+
+    def reduction_kind(self, node) -> str:
+        src = self.sizes(node.inputs[0])
+        axes = ir.normalise_axes(node.attrs["axes"], len(src))
+        if len(src) >= 1 and axes == (len(src) - 1,):
+            return "row"
+        if len(src) == 2 and axes == (0,):
+            return "col"
+        if axes == tuple(range(len(src))):
+            return "full"
+        return "naive"
+
+    # ------------------------------------------------------------------ gemm operands
+
+    def gemm_operand(self, name: str, want_int8: bool) -> tuple[str, bool, bool]:
+        """Peel transposes / no-op reshapes / int8->int32 casts: (base, flipped, from_int8)."""
+        cur, flipped, from_int8 = name, False, False
+        while True:
+            node = self.producers.get(cur)
+            if node is None:
+                break
+            op = node.op.name
+            if op == "transpose" and tuple(node.attrs["permutation"]) == (1, 0):
+                flipped = not flipped
+                cur = node.inputs[0]
+                continue
+            if op == "reshape" and self.sizes(node.inputs[0]) == self.sizes(cur):
+                cur = node.inputs[0]
+                continue
+            if op in ("print", "assert_finite"):
+                cur = node.inputs[0]
+                continue
+            if (
+                want_int8
+                and op == "cast"
+                and node.output.dtype.name == "int32"
+                and self.values[node.inputs[0]].dtype.name == "int8"
+            ):
+                from_int8 = True
+                cur = node.inputs[0]
+                continue
+            break
+        return cur, flipped, from_int8
+
+    # ------------------------------------------------------------------ partition
+
+    def partition(self) -> list[Step]:
+        produced_at: dict[str, int] = {n: -1 for n in self.inputs}
+        open_groups: dict[tuple[int, ...], RowGroup] = {}
+        raw: list[tuple[str, object]] = []  # ("gemm", node) | ("row", group) | ("red", node)
+
+        def close_all():
+            for g in list(open_groups.values()):
+                raw.append(("row", g))
+                for m in g.members:
+                    produced_at[m] = len(raw) - 1
+            open_groups.clear()
+
+        for node in self.order:
+            cat = node.op.category
+            if cat == ir.CONTRACTION:
+                close_all()
+                raw.append(("gemm", node))
+                produced_at[node.name] = len(raw) - 1
+            elif cat == ir.REDUCTION:
+                kind = self.reduction_kind(node)
+                if kind != "row":
+                    close_all()
+                    raw.append(("red", node))
+                    produced_at[node.name] = len(raw) - 1
+                    continue
+                src = node.inputs[0]
+                ss = self.sizes(src)
+                deps = self.hard_deps(src)
+                g = open_groups.get(ss)
+                if g is not None:
+                    outside = [d for d in deps if d not in g.members]
+                    ready = all(d in produced_at for d in outside)
+                    aligned = self._row_aligned(node, g)
+                    if ready and aligned:
+                        inner = [d for d in deps if d in g.members]
+                        g.phase[node.name] = 1 + max((g.phase[d] for d in inner), default=0)
+                        g.members.append(node.name)
+                        continue
+                    raw.append(("row", g))
+                    for m in g.members:
+                        produced_at[m] = len(raw) - 1
+                    del open_groups[ss]
+                if not all(d in produced_at for d in deps):
+                    close_all()
+                g = RowGroup([node.name], ss, {node.name: 1})
+                open_groups[ss] = g
+        close_all()
+        self.raw = raw
+        self.produced_at = produced_at
+        return self._build_steps()
+
+    def _row_aligned(self, node, group: RowGroup) -> bool:
+        """Whether ``node``'s source reads group members only at the current row."""
+        members = set(group.members)
+        ok = True
+        R = _prod(group.src_sizes[:-1])
+        row_idx = self._row_index(group.src_sizes)
+
+        def resolve(name, idx):
+            nonlocal ok
+            if name in members:
+                if tuple(idx) != self._reduced_row_index(name, row_idx):
+                    ok = False
+                return "0"
+            if self.is_hard(name):
+                return "0"
+            return None
+
+        eb = ExprBuilder(self.values, self.producers, lambda n: None, resolve)
+        try:
+            eb.value(node.inputs[0], row_idx + ("col",))
+        except CodegenError:
+            return False
+        del R
+        return ok
+
+    @staticmethod
+    def _row_index(src_sizes) -> tuple[str, ...]:
+        lead = src_sizes[:-1]
+        return tuple(delinearise("row", lead)) if lead else ()
+
+    def _reduced_row_index(self, name: str, row_idx: tuple[str, ...]) -> tuple[str, ...]:
+        node = self.producers[name]
+        keep = bool(node.attrs.get("keepdims", False))
+        return row_idx + ("0",) if keep else row_idx
+
+    # ------------------------------------------------------------------ requests and owners
+
+    def _build_steps(self) -> list[Step]:
+        # 1. requests: soft graph outputs and soft GEMM operand bases
+        requests: list[str] = []
+        gemm_ops: dict[str, tuple] = {}
+        for kind, obj in self.raw:
+            if kind != "gemm":
+                continue
+            node = obj
+            dt = node.output.dtype.name
+            if dt not in ("float32", "int32"):
+                raise CodegenError(f"matmul in {dt} has no tensor-core lowering on B200")
+            if len(self.sizes(node.inputs[0])) != 2 or len(self.sizes(node.inputs[1])) != 2:
+                raise CodegenError("batched matmul is not lowered by the B200 backend")
+            want_int8 = dt == "int32"
+            a = self.gemm_operand(node.inputs[0], want_int8)
+            b = self.gemm_operand(node.inputs[1], want_int8)
+            if want_int8 and not (a[2] and b[2]):
+                raise CodegenError("an int32 matmul lowers only when both operands are int8 values cast to int32")
+            if not want_int8 and (self.values[a[0]].dtype.name != "float32" or self.values[b[0]].dtype.name != "float32"):
+                raise CodegenError("a float32 matmul needs float32 operands")
+            gemm_ops[node.name] = (a, b)
+            for base, _, _ in (a, b):
+                if self.is_hard(base):
+                    if base not in self.inputs:
+                        self.materialised.add(base)
+                elif base not in requests:
+                    requests.append(base)
+        for o in self.outputs:
+            if self.is_hard(o):
+                if o not in self.inputs:
+                    self.materialised.add(o)
+            elif o not in requests:
+                requests.append(o)
+        self.gemm_ops = gemm_ops
+
+        # 2. owners
+        step_of: dict[str, int] = {}
+        for k, (kind, obj) in enumerate(self.raw):
+            if kind == "row":
+                for m in obj.members:
+                    step_of[m] = k
+            else:
+                step_of[obj.name] = k
+        owned: dict[int, list[str]] = {}
+        maps: dict[int, list[str]] = {}
+        for r in requests:
+            deps = self.hard_deps(r)
+            latest = max((step_of.get(d, -1) for d in deps), default=-1)
+            owner = None
+            if latest >= 0:
+                kind, obj = self.raw[latest]
+                rs = self.sizes(r)
+                if kind == "gemm" and rs == self.sizes(obj.name) and self._epilogue_ok(obj.name, r):
+                    owner = latest
+                elif kind == "row" and (rs == obj.src_sizes or rs in self._row_shapes(obj.src_sizes)):
+                    if self._final_phase_ok(obj, r):
+                        owner = latest
+            if owner is None:
+                maps.setdefault(latest, []).append(r)
+            else:
+                owned.setdefault(owner, []).append(r)
+
+        # 3. which hard values are read by a kernel other than their producer
+        def note_reads(names_for_kernel: list[str], own: set[str]):
+            for n in names_for_kernel:
+                for d in self.hard_deps(n):
+                    if d not in own and d not in self.inputs:
+                        self.materialised.add(d)
+
+        for k, (kind, obj) in enumerate(self.raw):
+            if kind == "gemm":
+                note_reads(owned.get(k, []), {obj.name})
+            elif kind == "row":
+                members = set(obj.members)
+                note_reads([self.producers[m].inputs[0] for m in obj.members], members)
+                note_reads(owned.get(k, []), members)
+            else:
+                note_reads([obj.inputs[0]], set())
+        for k, rs in maps.items():
+            note_reads(rs, set())
+
+        # 4. emit steps in order, map steps right after the step they depend on
+        steps: list[Step] = []
+        for r in maps.get(-1, []):
+            steps.append(self._map_step([r]))
+        for k, (kind, obj) in enumerate(self.raw):
+            if kind == "gemm":
+                steps.append(self._gemm_step(obj, owned.get(k, [])))
+            elif kind == "row":
+                steps.append(self._row_step(obj, owned.get(k, [])))
+            else:
+                steps.extend(self._reduction_steps(obj))
+            for r in maps.get(k, []):
+                steps.append(self._map_step([r]))
+        self.steps = steps
+        return steps
+
+    def _row_shapes(self, src_sizes) -> list[tuple[int, ...]]:
+        lead = tuple(src_sizes[:-1])
+        return [lead, lead + (1,)]
+
+    def _epilogue_ok(self, gemm: str, request: str) -> bool:
+        ok = True
+        ident = ("row", "col")
+
+        def resolve(name, idx):
+            nonlocal ok
+            if name == gemm:
+                if tuple(idx) != ident:
+                    ok = False
+                return "acc"
+            if self.is_hard(name):
+                return "0"
+            return None
+
+        eb = ExprBuilder(self.values, self.producers, lambda n: None, resolve)
+        try:
+            eb.value(request, ident)
+        except CodegenError:
+            return False
+        return ok
+
+    def _final_phase_ok(self, group: RowGroup, request: str) -> bool:
+        members = set(group.members)
+        row_idx = self._row_index(group.src_sizes)
+        rs = self.sizes(request)
+        full = rs == tuple(group.src_sizes)
+        idx = row_idx + ("col",) if full else (row_idx + ("0",) if rs == tuple(group.src_sizes[:-1]) + (1,) else row_idx)
+        ok = True
+
+        def resolve(name, i):
+            nonlocal ok
+            if name in members:
+                if tuple(i) != self._reduced_row_index(name, row_idx):
+                    ok = False
+                return "0"
+            if self.is_hard(name):
+                if not full:
+                    # a row-shaped output may only read per-row values
+                    ok = False
+                return "0"
+            return None
+
+        eb = ExprBuilder(self.values, self.producers, lambda n: None, resolve)
+        try:
+            eb.value(request, idx)
+        except CodegenError:
+            return False
+        return ok
+
+    # ------------------------------------------------------------------ kernel sources
+
+    def _kname(self, stem: str) -> str:
+        self.kernel_count += 1
+        return f"tgcb_{stem}_{self.kernel_count}"
+
+    def _pointer_of(self, name: str) -> str | None:
+        if name in self.inputs or name in self.materialised:
+            return PTR(name)
+        return None
+
+    def _map_step(self, names: list[str]) -> Step:
+        out_sizes = self.sizes(names[0])
+        total = max(1, _prod(out_sizes))
+        kname = self._kname("map")
+        body: list[str] = []
+        reads: set[str] = set()
+        T = 256
+        unroll = 4
+        for u in range(unroll):
+            e = f"(base + {u}LL * stride)"
+            idx = tuple(delinearise(e, out_sizes)) if out_sizes else ()
+            eb = ExprBuilder(self.values, self.producers, self._pointer_of, indent="      ")
+            stores = []
+            for n in names:
+                v = eb.value(n, idx)
+                stores.append(f"      reinterpret_cast<{ctype(self.values[n].dtype)}*>({PTR(n)})[{e}] = {v};")
+            reads |= eb.loads
+            body.append(f"    if ({e} < {total}LL) {{")
+            body.extend(eb.lines)
+            body.extend(stores)
+            body.append("    }")
+        blocks = max(1, min((total + T * unroll - 1) // (T * unroll), NUM_SMS * 16))
+        src = (
+            f'extern "C" __global__ void __launch_bounds__({T}) {kname}(const TgcbArgs args) {{\n'
+            f"  const long long stride = (long long)gridDim.x * blockDim.x;\n"
+            f"  for (long long base = (long long)blockIdx.x * blockDim.x + threadIdx.x; base < {total}LL;"
+            f" base += {unroll}LL * stride) {{\n" + "\n".join(body) + "\n  }\n}\n"
+        )
+        return Step(
+            "map",
+            ",".join(names),
+            reads=sorted(reads),
+            writes=list(names),
+            source=src,
+            launches=[Launch(kname, (blocks, 1, 1), (T, 1, 1))],
+            nodes=list(names),
+        )
+
+    def _row_step(self, group: RowGroup, requests: list[str]) -> Step:
+        ss = tuple(group.src_sizes)
+        C = ss[-1]
+        R = _prod(ss[:-1])
+        T = row_threads(C)
+        W = T // 32
+        npt = (C + T - 1) // T
+        unrolled = npt <= 32
+        members = group.members
+        members_set = set(members)
+        max_phase = max(group.phase.values())
+        row_idx = self._row_index(ss)
+        kname = self._kname("row")
+        full_req = [r for r in requests if self.sizes(r) == ss]
+        row_req = [r for r in requests if self.sizes(r) != ss]
+        reads: set[str] = set()
+        lines: list[str] = []
+        nred = len(members)
+        slot = {m: k for k, m in enumerate(members)}
+
+        def member_resolve(name, idx):
+            if name in members_set:
+                return f"red_{slot[name]}"
+            return None
+
+        shared_eb = ExprBuilder(self.values, self.producers, self._pointer_of, member_resolve, indent="    ")
+
+        def col_expr(k):
+            return f"((long long)threadIdx.x + {k * T}LL)" if unrolled else "col"
+
+        for phase in range(1, max_phase + 1):
+            pm = [m for m in members if group.phase[m] == phase]
+            accs = {}
+            for m in pm:
+                node = self.producers[m]
+                t = ctype(node.output.dtype)
+                src_t = ctype(self.values[node.inputs[0]].dtype)
+                if node.op.name == "max":
+                    init = "-INFINITY" if t in ("float", "double") else ("(-2147483647-1)" if t == "int" else "(-9223372036854775807LL-1)")
+                else:
+                    init = f"({t})0"
+                accs[m] = (f"acc_{slot[m]}", t, node.op.name, src_t)
+                lines.append(f"    {t} acc_{slot[m]} = {init};")
+            if unrolled:
+                eb = shared_eb
+                ks = range(npt)
+            else:
+                eb = ExprBuilder(self.values, self.producers, self._pointer_of, member_resolve, indent="      ")
+                ks = [0]
+                lines.append(f"    for (long long col = threadIdx.x; col < {C}LL; col += {T}LL) {{")
+            for k in ks:
+                col = col_expr(k)
+                colc = f"tgcb_min_ll({col}, {C - 1}LL)" if (unrolled and C % T) else col
+                for m in pm:
+                    node = self.producers[m]
+                    v = eb.value(node.inputs[0], row_idx + (colc,))
+                    acc, t, opn, _ = accs[m]
+                    if opn == "max":
+                        upd = f"(({acc}) != ({acc}) || ({acc}) > ({v})) ? ({acc}) : ({t})({v})"
+                    else:
+                        upd = f"{acc} + ({t})({v})"
+                    guard = f"({col} < {C}LL) ? ({upd}) : {acc}" if (unrolled and C % T) else upd
+                    eb.emit(f"{acc} = {guard};")
+                if unrolled:
+                    lines.extend(eb.lines)
+                    eb.lines = []
+            if not unrolled:
+                lines.extend(eb.lines)
+                lines.append("    }")
+            # block-level combine of this phase's accumulators, declared tree bracketing
+            for m in pm:
+                acc, t, opn, _ = accs[m]
+                fn = "tgcb_block_max" if opn == "max" else "tgcb_block_sum"
+                lines.append(f"    {t} red_{slot[m]} = {fn}<{t}, {W}>({acc}, reinterpret_cast<{t}*>(red_smem[{slot[m]}]));")
+                if opn == "mean":
+                    lines.append(f"    red_{slot[m]} = red_{slot[m]} / ({t}){C};")
+            lines.append("    __syncthreads();")
+        # final phase: full-shaped requests
+        if full_req:
+            if unrolled:
+                eb = shared_eb
+                for k in range(npt):
+                    col = col_expr(k)
+                    colc = f"tgcb_min_ll({col}, {C - 1}LL)" if C % T else col
+                    for r in full_req:
+                        v = eb.value(r, row_idx + (colc,))
+                        st = f"reinterpret_cast<{ctype(self.values[r].dtype)}*>({PTR(r)})[row * {C}LL + {col}] = {v};"
+                        eb.emit(f"if ({col} < {C}LL) {st}" if C % T else st)
+                    lines.extend(eb.lines)
+                    eb.lines = []
+            else:
+                eb = ExprBuilder(self.values, self.producers, self._pointer_of, member_resolve, indent="      ")
+                lines.append(f"    for (long long col = threadIdx.x; col < {C}LL; col += {T}LL) {{")
+                for r in full_req:
+                    v = eb.value(r, row_idx + ("col",))
+                    eb.emit(f"reinterpret_cast<{ctype(self.values[r].dtype)}*>({PTR(r)})[row * {C}LL + col] = {v};")
+                lines.extend(eb.lines)
+                lines.append("    }")
+        # per-row results: materialised reductions and row-shaped requests
+        row_stores = [m for m in members if m in self.materialised] + row_req
+        if row_stores:
+            eb = ExprBuilder(self.values, self.producers, self._pointer_of, member_resolve, indent="      ")
+            lines.append("    if (threadIdx.x == 0) {")
+            for r in row_stores:
+                rs = self.sizes(r)
+                idx = row_idx + ("0",) if len(rs) == len(ss) else row_idx
+                v = eb.value(r, idx)
+                eb.emit(f"reinterpret_cast<{ctype(self.values[r].dtype)}*>({PTR(r)})[row] = {v};")
+            lines.extend(eb.lines)
+            lines.append("    }")
+        reads |= shared_eb.loads
+        grid = max(1, min(R, NUM_SMS * max(1, 2048 // T) * 2))
+        src = (
+            f'extern "C" __global__ void __launch_bounds__({T}) {kname}(const TgcbArgs args) {{\n'
+            f"  __shared__ double red_smem[{nred}][{W}];\n"
+            f"  for (long long row = blockIdx.x; row < {R}LL; row += gridDim.x) {{\n"
+            + "\n".join(lines)
+            + "\n  }\n}\n"
+        )
+        writes = [m for m in members if m in self.materialised] + list(requests)
+        for m in members:
+            for d in self.hard_deps(self.producers[m].inputs[0]):
+                if d not in members_set:
+                    reads.add(d)
+        for r in requests:
+            for d in self.hard_deps(r):
+                if d not in members_set:
+                    reads.add(d)
+        return Step(
+            "row",
+            ",".join(members),
+            reads=sorted(reads),
+            writes=writes,
+            source=src,
+            launches=[Launch(kname, (grid, 1, 1), (T, 1, 1))],
+            bracketing=f"row tree: {T} threads, thread t sums columns t, t+{T}, ... in order; "
+            f"lanes combined by xor tree (1,2,4,8,16); {W} warp partials combined as a balanced tree",
+            nodes=list(members) + list(requests),
+        )
+
+    def _reduction_steps(self, node) -> list[Step]:
+        kind = self.reduction_kind(node)
+        if kind == "col":
+            return self._col_steps(node)
+        if kind == "full":
+            return self._full_steps(node)
+        return [self._naive_step(node)]
+
+    def _acc_update(self, opn: str, acc: str, v: str, t: str) -> str:
+        if opn == "max":
+            return f"{acc} = (({acc}) != ({acc}) || ({acc}) > ({v})) ? ({acc}) : ({t})({v});"
+        return f"{acc} = {acc} + ({t})({v});"
+
+    def _init(self, opn: str, t: str) -> str:
+        if opn == "max":
+            return "-INFINITY" if t in ("float", "double") else "(-2147483647-1)"
+        return f"({t})0"
+
+    def _col_steps(self, node) -> list[Step]:
+        """Reduction over axis 0 of [R, C]: P row partitions summed sequentially, then the P partials in order."""
+        name = node.name
+        src = node.inputs[0]
+        R, C = self.sizes(src)
+        t = ctype(node.output.dtype)
+        opn = node.op.name
+        cblocks = (C + 255) // 256
+        P = max(1, min((R + 15) // 16, (NUM_SMS * 4 + cblocks - 1) // cblocks))
+        L = (R + P - 1) // P
+        P = (R + L - 1) // L
+        scratch = f"{name}__partials"
+        self.scratch[scratch] = P * C * 8
+        k1, k2 = self._kname("colpart"), self._kname("colfinal")
+        eb = ExprBuilder(self.values, self.producers, self._pointer_of, indent="    ")
+        v = eb.value(src, ("r", "c"))
+        body = "\n".join(eb.lines)
+        s1 = (
+            f'extern "C" __global__ void __launch_bounds__(256) {k1}(const TgcbArgs args) {{\n'
+            f"  const long long c = (long long)blockIdx.x * 256 + threadIdx.x;\n"
+            f"  if (c >= {C}LL) return;\n"
+            f"  const long long r0 = (long long)blockIdx.y * {L}LL;\n"
+            f"  const long long r1 = min(r0 + {L}LL, {R}LL);\n"
+            f"  {t} acc = {self._init(opn, t)};\n"
+            f"  for (long long r = r0; r < r1; ++r) {{\n{body}\n    {self._acc_update(opn, 'acc', v, t)}\n  }}\n"
+            f"  reinterpret_cast<{t}*>({PTR(scratch)})[blockIdx.y * {C}LL + c] = acc;\n}}\n"
+        )
+        fin = f"acc / ({t}){R}" if opn == "mean" else "acc"
+        s2 = (
+            f'extern "C" __global__ void __launch_bounds__(256) {k2}(const TgcbArgs args) {{\n'
+            f"  const long long c = (long long)blockIdx.x * 256 + threadIdx.x;\n"
+            f"  if (c >= {C}LL) return;\n"
+            f"  const {t}* part = reinterpret_cast<const {t}*>({PTR(scratch)});\n"
+            f"  {t} acc = {self._init(opn, t)};\n"
+            f"  for (int p = 0; p < {P}; ++p) {{ const {t} v = part[p * {C}LL + c]; {self._acc_update(opn, 'acc', 'v', t)} }}\n"
+            f"  reinterpret_cast<{t}*>({PTR(name)})[c] = {fin};\n}}\n"
+        )
+        reads = sorted(d for d in self.hard_deps(src) if d != name)
+        self.materialised.add(name)
+        return [
+            Step(
+                "colreduce",
+                name,
+                reads=reads,
+                writes=[scratch, name],
+                source=s1 + "\n" + s2,
+                launches=[
+                    Launch(k1, (cblocks, P, 1), (256, 1, 1)),
+                    Launch(k2, (cblocks, 1, 1), (256, 1, 1)),
+                ],
+                bracketing=f"partitioned: {P} row blocks of {L} summed sequentially, then the {P} partials in order",
+                nodes=[name],
+            )
+        ]
+
+    def _full_steps(self, node) -> list[Step]:
+        """Reduction over every axis: G contiguous chunks, each a block tree, then a tree over G."""
+        name = node.name
+        src = node.inputs[0]
+        ss = self.sizes(src)
+        n = max(1, _prod(ss))
+        t = ctype(node.output.dtype)
+        opn = node.op.name
+        T = 256
+        G = max(1, min(NUM_SMS * 4, (n + T * 8 - 1) // (T * 8)))
+        chunk = (n + G - 1) // G
+        G = (n + chunk - 1) // chunk
+        scratch = f"{name}__partials"
+        self.scratch[scratch] = G * 8
+        k1, k2 = self._kname("fullpart"), self._kname("fullfinal")
+        eb = ExprBuilder(self.values, self.producers, self._pointer_of, indent="    ")
+        v = eb.value(src, tuple(delinearise("e", ss)) if ss else ())
+        body = "\n".join(eb.lines)
+        fn = "tgcb_block_max" if opn == "max" else "tgcb_block_sum"
+        s1 = (
+            f'extern "C" __global__ void __launch_bounds__({T}) {k1}(const TgcbArgs args) {{\n'
+            f"  __shared__ double red_smem[{T // 32}];\n"
+            f"  const long long e0 = (long long)blockIdx.x * {chunk}LL;\n"
+            f"  const long long e1 = min(e0 + {chunk}LL, {n}LL);\n"
+            f"  {t} acc = {self._init(opn, t)};\n"
+            f"  for (long long e = e0 + threadIdx.x; e < e1; e += {T}LL) {{\n{body}\n    {self._acc_update(opn, 'acc', v, t)}\n  }}\n"
+            f"  acc = {fn}<{t}, {T // 32}>(acc, reinterpret_cast<{t}*>(red_smem));\n"
+            f"  if (threadIdx.x == 0) reinterpret_cast<{t}*>({PTR(scratch)})[blockIdx.x] = acc;\n}}\n"
+        )
+        fin = f"acc / ({t}){n}" if opn == "mean" else "acc"
+        s2 = (
+            f'extern "C" __global__ void __launch_bounds__({T}) {k2}(const TgcbArgs args) {{\n'
+            f"  __shared__ double red_smem[{T // 32}];\n"
+            f"  const {t}* part = reinterpret_cast<const {t}*>({PTR(scratch)});\n"
+            f"  {t} acc = {self._init(opn, t)};\n"
+            f"  for (int g = threadIdx.x; g < {G}; g += {T}) {{ const {t} v = part[g]; {self._acc_update(opn, 'acc', 'v', t)} }}\n"
+            f"  acc = {fn}<{t}, {T // 32}>(acc, reinterpret_cast<{t}*>(red_smem));\n"
+            f"  if (threadIdx.x == 0) reinterpret_cast<{t}*>({PTR(name)})[0] = {fin};\n}}\n"
+        )
+        reads = sorted(d for d in self.hard_deps(src) if d != name)
+        self.materialised.add(name)
+        return [
+            Step(
+                "fullreduce",
+                name,
+                reads=reads,
+                writes=[scratch, name],
+                source=s1 + "\n" + s2,
+                launches=[Launch(k1, (G, 1, 1), (T, 1, 1)), Launch(k2, (1, 1, 1), (T, 1, 1))],
+                bracketing=f"{G} chunks of {chunk}: thread-strided sequential sums, block tree per chunk, "
+                f"then thread-strided sums of the partials and one block tree",
+                nodes=[name],
+            )
+        ]
+
+    def _naive_step(self, node) -> Step:
+        """Any other axis set: one thread per output element, sequential over the reduced indices."""
+        name = node.name
+        src = node.inputs[0]
+        ss = self.sizes(src)
+        axes = ir.normalise_axes(node.attrs["axes"], len(ss))
+        keep = bool(node.attrs.get("keepdims", False))
+        kept_axes = [a for a in range(len(ss)) if a not in axes]
+        out_n = max(1, _prod([ss[a] for a in kept_axes]))
+        red_sizes = [ss[a] for a in axes]
+        red_n = max(1, _prod(red_sizes))
+        t = ctype(node.output.dtype)
+        opn = node.op.name
+        kname = self._kname("reduce")
+        out_idx = delinearise("o", [ss[a] for a in kept_axes]) if kept_axes else ()
+        red_idx = delinearise("q", red_sizes) if red_sizes else ()
+        full_idx = [""] * len(ss)
+        for a, e in zip(kept_axes, out_idx, strict=True):
+            full_idx[a] = e
+        for a, e in zip(axes, red_idx, strict=True):
+            full_idx[a] = e
+        eb = ExprBuilder(self.values, self.producers, self._pointer_of, indent="    ")
+        v = eb.value(src, tuple(full_idx))
+        fin = f"acc / ({t}){red_n}" if opn == "mean" else "acc"
+        src_code = (
+            f'extern "C" __global__ void __launch_bounds__(256) {kname}(const TgcbArgs args) {{\n'
+            f"  const long long o = (long long)blockIdx.x * 256 + threadIdx.x;\n"
+            f"  if (o >= {out_n}LL) return;\n"
+            f"  {t} acc = {self._init(opn, t)};\n"
+            f"  for (long long q = 0; q < {red_n}LL; ++q) {{\n" + "\n".join(eb.lines)
+            + f"\n    {self._acc_update(opn, 'acc', v, t)}\n  }}\n"
+            f"  reinterpret_cast<{t}*>({PTR(name)})[o] = {fin};\n}}\n"
+        )
+        del keep
+        self.materialised.add(name)
+        return Step(
+            "reduce",
+            name,
+            reads=sorted(d for d in self.hard_deps(src) if d != name),
+            writes=[name],
+            source=src_code,
+            launches=[Launch(kname, ((out_n + 255) // 256, 1, 1), (256, 1, 1))],
+            bracketing="sequential over the reduced indices in row-major order",
+            nodes=[name],
+        )
+
+    # ------------------------------------------------------------------ gemm
+
+    def _gemm_step(self, node, requests: list[str]) -> Step:
+        name = node.name
+        (a_base, a_flip, _), (b_base, b_flip, _) = self.gemm_ops[name]
+        M, K = self.sizes(node.inputs[0])
+        _, N = self.sizes(node.inputs[1])
+        is_int = node.output.dtype.name == "int32"
+        eb_bytes = 1 if is_int else 4
+        a_rows, a_cols = self.sizes(a_base)
+        b_rows, b_cols = self.sizes(b_base)
+        # A is [M, K]: row-major base [M, K] is K-major; a flipped base [K, M] is M-major.
+        opa = GemmOperand(a_base, a_rows, a_cols, a_flip, eb_bytes)
+        # B is [K, N]: row-major base [K, N] is N-major; a flipped base [N, K] is K-major.
+        opb = GemmOperand(b_base, b_rows, b_cols, not b_flip, eb_bytes)
+        stores = list(requests)
+        if name in self.materialised:
+            stores.insert(0, name)
+        kname = self._kname("gemm")
+        acc_t = "int" if is_int else "float"
+        chunk = 16
+
+        lines = []
+        for j in range(chunk):
+            col = f"(col0 + {j})"
+
+            def resolve(n, idx, col=col):
+                if n == name:
+                    return f"acc[{j}]"
+                return None
+
+            eb = ExprBuilder(self.values, self.producers, self._pointer_of, resolve, indent="      ")
+            st = []
+            for r in stores:
+                v = eb.value(r, ("row", col))
+                st.append(f"      reinterpret_cast<{ctype(self.values[r].dtype)}*>({PTR(r)})[row * {N}LL + {col}] = {v};")
+            lines.append(f"    if ({col} < {N}LL) {{")
+            lines.extend(eb.lines)
+            lines.extend(st)
+            lines.append("    }")
+        epi_name = f"Epi_{kname}"
+        epi = (
+            f"struct {epi_name} {{\n"
+            f"  static __device__ __forceinline__ void apply(const TgcbArgs& args, long long row, long long col0, const {acc_t} (&acc)[{chunk}]) {{\n"
+            f"    if (row >= {M}LL) return;\n" + "\n".join(lines) + "\n  }\n};\n"
+        )
+        reads = {a_base, b_base}
+        for r in requests:
+            for d in self.hard_deps(r):
+                if d != name:
+                    reads.add(d)
+        tma_ok = all((op.cols * op.elem_bytes) % 16 == 0 for op in (opa, opb))
+        if tma_ok:
+            kernel = (
+                f'extern "C" __global__ void __launch_bounds__(320, 1) {kname}(const TgcbArgs args, '
+                "const __grid_constant__ TgcbTmaDesc ta, const __grid_constant__ TgcbTmaDesc tb) {\n"
+                f"  tgcb_gemm::gemm_body<{M}, {N}, {K}, {'true' if is_int else 'false'}, "
+                f"{'true' if opa.mn_major else 'false'}, {'true' if opb.mn_major else 'false'}, {epi_name}>(args, &ta, &tb);\n}}\n"
+            )
+            tiles = ((M + 127) // 128) * ((N + 255) // 256)
+            launch = Launch(kname, (max(1, min(tiles, NUM_SMS)), 1, 1), (320, 1, 1), smem=-1, gemm=(opa, opb))
+            how = "tcgen05." + ("kind::i8, int32 accumulator in TMEM (exact)" if is_int else "kind::tf32, fp32 accumulator in TMEM, K in steps of 8")
+        else:
+            kernel = self._gemm_simt_kernel(kname, epi_name, M, N, K, is_int, a_base, a_flip, b_base, b_flip)
+            launch = Launch(kname, ((M * ((N + 15) // 16) + 127) // 128, 1, 1), (128, 1, 1))
+            how = "SIMT fallback for rows TMA cannot tile: sequential over K with tf32-truncated operands"
+        return Step(
+            "gemm",
+            name,
+            reads=sorted(reads),
+            writes=stores,
+            source=epi + kernel,
+            launches=[launch],
+            bracketing=how,
+            nodes=[name] + list(requests),
+        )
+
+    def _gemm_simt_kernel(self, kname, epi_name, M, N, K, is_int, a_base, a_flip, b_base, b_flip) -> str:
+        """One thread per 16 output columns of a row; used when an operand row is not 16-byte aligned."""
+        et = "signed char" if is_int else "float"
+        at = "int" if is_int else "float"
+        a_idx = "(long long)k * %dLL + row" % M if a_flip else "row * %dLL + k" % K
+        b_idx = "(long long)(col0 + j) * %dLL + k" % K if b_flip else "(long long)k * %dLL + col0 + j" % N
+        if is_int:
+            load_a = f"(int)reinterpret_cast<const {et}*>({PTR(a_base)})[{a_idx}]"
+            load_b = f"(int)reinterpret_cast<const {et}*>({PTR(b_base)})[{b_idx}]"
+            fma = "acc[j] = (int)((unsigned int)acc[j] + (unsigned int)(a * b));"
+        else:
+            trunc = "__uint_as_float(__float_as_uint(%s) & 0xffffe000u)"
+            load_a = trunc % f"reinterpret_cast<const {et}*>({PTR(a_base)})[{a_idx}]"
+            load_b = trunc % f"reinterpret_cast<const {et}*>({PTR(b_base)})[{b_idx}]"
+            fma = "acc[j] = fmaf(a, b, acc[j]);"
+        groups = (N + 15) // 16
+        return (
+            f'extern "C" __global__ void __launch_bounds__(128) {kname}(const TgcbArgs args) {{\n'
+            f"  const long long t = (long long)blockIdx.x * 128 + threadIdx.x;\n"
+            f"  if (t >= {M}LL * {groups}LL) return;\n"
+            f"  const long long row = t / {groups}LL;\n"
+            f"  const long long col0 = (t % {groups}LL) * 16;\n"
+            f"  {at} acc[16];\n"
+            f"  for (int j = 0; j < 16; ++j) acc[j] = 0;\n"
+            f"  for (int k = 0; k < {K}; ++k) {{\n"
+            f"    const {at} a = {load_a};\n"
+            f"    for (int j = 0; j < 16; ++j) {{\n"
+            f"      if (col0 + j < {N}LL) {{ const {at} b = {load_b}; {fma} }}\n"
+            f"    }}\n  }}\n"
+            f"  {epi_name}::apply(args, row, col0, acc);\n}}\n"
+        )
+
+
+def lower(graph, order) -> Lowering:
+    low = Lowering(graph, order)
+    low.partition()
+    return low
+
+
+def gemm_flops(steps: list[Step], lowering: Lowering) -> int:
+    """2*M*N*K summed over the GEMM steps."""
+    total = 0
+    for s in steps:
+        if s.kind == "gemm":
+            node = lowering.producers[s.label]
+            M, K = lowering.sizes(node.inputs[0])
+            N = lowering.sizes(node.inputs[1])[1]
+            total += 2 * M * N * K
+    return total
+
+
+_ = (math, _broadcast_index)
