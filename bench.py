@@ -1,0 +1,669 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 backend on tgc's workloads; prints ONE JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl tgcb|reference] [--workload NAME]
+
+Default workload ``mlp``: the transformer MLP block (layernorm -> x@W1+b1 -> tanh-form GELU
+-> @W2+b2; x [8192,1024], W1 [1024,4096], W2 [4096,1024], fp32 with TF32 tensor-core GEMMs),
+compiled by ``tgcb.runtime.compile_graph`` from tgc's graph and run as three kernels. A
+step is one execution of the compiled graph. Other workloads: ``cone`` (x [4096,1024] ->
+exp -> three row reductions), ``int8`` (per-token/per-channel int8 linear
+8192x4096x4096), ``longsum`` (bit-exact pairwise sum of 2^26 floats).
+
+Multi-GPU (torchrun, one process per GPU, NCCL): every rank runs its own shard of rows, so
+work per GPU is fixed ("weak"); ``value`` = executions by all ranks / the slowest rank's
+device time. Timing: W warm-up steps; then K steps, each timed with CUDA events recorded on
+the stream the kernels run on (one event around every kernel, tgcb_plan_run_profiled); L2
+flushed before every timed step outside the events (a 256 MiB write, then a 256 MiB read so
+the flush leaves no dirty lines to be written back inside a timed kernel); a bounded delay
+kernel queued ahead of each step so its launches start back to back; barrier + synchronize
+on both sides; the max over ranks.
+
+``e2e`` times the same step through the public API with host buffers: every step copies all
+inputs from pinned host memory into the arena and reads the results back to pinned host
+memory inside the timed region.
+
+``--impl reference`` times tgc's own CPU path restated by oracle/ (the generated-Python
+executor: one torch CPU op per node into one arena) on the host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "tensor-graph-compiler_b200"))
+sys.path.insert(0, REPO)
+
+METRIC = "fused-graph execs/sec and achieved HBM GB/s (% of peak) at 1/2/4/8 B200"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_FLUSH_BYTES = 256 << 20
+L2_NOTE = (
+    "flushed before every timed step: 256 MiB write, then a 256 MiB read so no dirty flush "
+    "lines are written back inside the timed kernels"
+)
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["tgcb", "reference"], default="tgcb")
+    p.add_argument("--workload", choices=["mlp", "cone", "int8", "longsum"], default="mlp")
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def peaks() -> tuple[dict, str]:
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi queried every 200 ms (read-only); summarises the samples of the timed region.
+
+    Started before the warm-up so sampling is running when timing begins; ``mark_start`` and
+    ``mark_end`` bracket the timed region in wall time. The samples inside it, plus the
+    nearest one on each side (a region shorter than the period still gets readings), are
+    summarised.
+    """
+
+    FIELDS = (
+        "timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+        "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[tuple[float, str]] = []
+        self.t0 = self.t1 = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except OSError:
+            self.proc = None
+            return
+        first = threading.Event()
+
+        def reader():
+            for line in self.proc.stdout:
+                self.lines.append((time.time(), line.strip()))
+                first.set()
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        first.wait(timeout=10)
+
+    def mark_start(self) -> None:
+        self.t0 = time.time()
+
+    def mark_end(self) -> None:
+        self.t1 = time.time()
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=5)
+        t0, t1 = self.t0 or 0.0, self.t1 or time.time()
+        inside = [ln for ts, ln in self.lines if t0 <= ts <= t1]
+        before = [ln for ts, ln in self.lines if ts < t0][-1:]
+        after = [ln for ts, ln in self.lines if ts > t1][:1]
+        sm, mx, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in before + inside + after:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9], strict=True):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {
+            "sm_mhz": statistics.median(sm),
+            "sm_max_mhz": max(mx),
+            "power_w_max": max(power) if power else None,
+            "samples": len(sm),
+            "samples_inside_timed_region": len(inside),
+            "reasons": sorted(reasons),
+        }
+
+
+# ----------------------------------------------------------------------------- workloads
+
+
+class GraphWorkload:
+    """A workload that is one tgc graph compiled by tgcb.runtime.compile_graph."""
+
+    name = ""
+    unit = "execs/s"
+    dtype = ""
+
+    def __init__(self, rank: int):
+        self.rank = rank
+
+    def graph(self):
+        raise NotImplementedError
+
+    def feeds(self) -> dict:
+        raise NotImplementedError
+
+    def config(self) -> dict:
+        raise NotImplementedError
+
+    def setup(self, device) -> None:
+        import torch
+
+        from tgcb.runtime import compile_graph
+
+        self.g = self.graph()
+        self.compiled = compile_graph(self.g, device=device.index)
+        self.cpu_feeds = self.feeds()
+        self.dev_feeds = {k: v.to(device) for k, v in self.cpu_feeds.items()}
+        self.host_feeds = {k: v.pin_memory() for k, v in self.cpu_feeds.items()}
+        self.arena = self.compiled.new_arena()
+        self.out_host = [
+            torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in self.compiled.function(self.arena, self.dev_feeds)
+        ]
+        torch.cuda.synchronize()
+        self.compiled.check_status()
+
+    def launches_per_step(self) -> int:
+        return self.compiled.launches_per_call
+
+    def step_profiled(self) -> list[float]:
+        return self.compiled.run_profiled(self.arena, self.dev_feeds)[1]
+
+    def step_e2e(self) -> None:
+        outs = self.compiled.function(self.arena, self.host_feeds)
+        for o, h in zip(outs, self.out_host, strict=True):
+            h.copy_(o, non_blocking=True)
+
+    def h2d_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self.host_feeds.values())
+
+    def d2h_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self.out_host)
+
+    def kernel_work(self) -> list[dict]:
+        """Per launch: name, kind, roofline bound and algorithmic work (bytes or ops)."""
+        low = self.compiled.lowering
+        out = []
+        for s in self.compiled.module.steps:
+            if s.kind == "gemm":
+                node = low.producers[s.label]
+                M, K = low.sizes(node.inputs[0])
+                N = low.sizes(node.inputs[1])[1]
+                is_int = node.output.dtype.name == "int32"
+                for ln in s.launches:
+                    out.append({"name": ln.kernel, "kind": s.kind, "bound": "tensor", "work": 2 * M * N * K,
+                                "type": "int8" if is_int else "tf32"})
+                continue
+            rbytes = sum(low.values[r].bytes for r in s.reads if r in low.values)
+            wbytes = sum(low.values[w].bytes for w in s.writes if w in low.values)
+            for i, ln in enumerate(s.launches):
+                out.append({"name": ln.kernel, "kind": s.kind, "bound": "hbm", "work": rbytes + wbytes if i == 0 else 0})
+        return out
+
+    def cpu_program(self):
+        from oracle import interp
+
+        return interp.generated_python_program(self.g)
+
+
+class MlpWorkload(GraphWorkload):
+    name = "mlp"
+    dtype = "tf32"
+    rows = 8192
+
+    def graph(self):
+        from tgcb import ir, workloads
+
+        return workloads.mlp_graph(ir.Builder, rows=self.rows)
+
+    def feeds(self):
+        from tgcb import workloads
+
+        return workloads.mlp_inputs(rows=self.rows, seed=self.rank)
+
+    def config(self):
+        return {
+            "workload": "transformer MLP block: layernorm(gamma=1,beta=0) -> x@W1+b1 -> GELU(tanh form) -> @W2+b2; "
+            "x [8192,1024] ~N(0,1), W1 [1024,4096], W2 [4096,1024] ~N(0,0.02), zero biases; fp32 graph, TF32 GEMMs",
+            "rows_per_gpu": self.rows,
+            "flops_per_exec": 2 * self.rows * 1024 * 4096 * 2,
+            "l2": L2_NOTE,
+        }
+
+
+class ConeWorkload(GraphWorkload):
+    name = "cone"
+    dtype = "f32"
+
+    def graph(self):
+        from tgcb import ir, workloads
+
+        return workloads.cone_graph(ir.Builder)
+
+    def feeds(self):
+        from tgcb import workloads
+
+        return workloads.cone_inputs(seed=self.rank)
+
+    def config(self):
+        return {
+            "workload": "fused cone: t=exp(0.5*x-1) over x [4096,1024] fp32 ~N(0,1); row-sum(t), row-max(t), row-sum(t*x)",
+            "bytes_per_exec": 4096 * 1024 * 4 + 3 * 4096 * 4,
+            "l2": L2_NOTE,
+        }
+
+
+class Int8Workload(GraphWorkload):
+    name = "int8"
+    dtype = "int8 x int8 -> int32, f32 dequant"
+
+    def graph(self):
+        from tgcb import ir, workloads
+
+        return workloads.int8_linear_graph(ir.Builder, ir.INT8, ir.INT32, ir.FLOAT32)
+
+    def feeds(self):
+        import torch
+
+        from oracle import quantize as oq
+        from tgcb import workloads
+
+        ins = workloads.int8_inputs(seed=self.rank)
+        qa, sa = oq.quantise_rows(ins["a"].numpy())
+        qwt, sw = oq.quantise_rows(ins["w"].T.contiguous().numpy())
+        return {"qa": torch.from_numpy(qa), "qwt": torch.from_numpy(qwt),
+                "sa": torch.from_numpy(sa).reshape(-1, 1), "sw": torch.from_numpy(sw).reshape(1, -1)}
+
+    def config(self):
+        return {"workload": "int8 linear: qa [8192,4096] x qwt^T [4096,4096] -> int32 acc -> *sa *sw (f32)",
+                "int_ops_per_exec": 2 * 8192 * 4096 * 4096, "l2": L2_NOTE}
+
+    def cpu_program(self):
+        from oracle import interp
+
+        g = self.g
+        return lambda feeds: interp.run(g, feeds)
+
+
+class LongSumWorkload:
+    """Pairwise (block 8) float32 sum of 2^26 values, bit-exact to tgc's summation.pairwise."""
+
+    name = "longsum"
+    unit = "sums/s"
+    dtype = "f32"
+    n = 1 << 26
+
+    def __init__(self, rank: int):
+        self.rank = rank
+
+    def config(self):
+        return {"workload": "pairwise (block 8) sum of 2^26 fp32 values ~U(0,1) with one 1e8 entry",
+                "bytes_per_sum": self.n * 4, "l2": L2_NOTE}
+
+    def setup(self, device):
+        import torch
+
+        from tgcb import summation, workloads
+
+        self.v, _ = workloads.longsum_input(self.n, seed=self.rank)
+        self.dev = self.v.to(device)
+        self.host = self.v.pin_memory()
+        self.out = torch.empty(1, dtype=torch.float32, device=device)
+        self.out_host = torch.empty(1, dtype=torch.float32).pin_memory()
+        self.scratch = torch.empty(summation.scratch_bytes(self.n), dtype=torch.uint8, device=device)
+        self.staging = torch.empty_like(self.dev)
+
+    def launches_per_step(self) -> int:
+        return 3  # leaves, then two combine levels for 2^23 nodes
+
+    def step_profiled(self) -> list[float]:
+        import torch
+
+        from tgcb import summation
+
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        summation.pairwise_into(self.dev, self.out, self.scratch)
+        e.record()
+        e.synchronize()
+        return [s.elapsed_time(e)]
+
+    def step_e2e(self) -> None:
+        from tgcb import summation
+
+        self.staging.copy_(self.host, non_blocking=True)
+        summation.pairwise_into(self.staging, self.out, self.scratch)
+        self.out_host.copy_(self.out, non_blocking=True)
+
+    def h2d_bytes(self) -> int:
+        return self.n * 4
+
+    def d2h_bytes(self) -> int:
+        return 4
+
+    def kernel_work(self) -> list[dict]:
+        return [{"name": "pairwise_leaves+pairwise_combine", "kind": "longsum", "bound": "hbm", "work": self.n * 4}]
+
+    def cpu_program(self):
+        from oracle import bracketing
+
+        v = self.v.numpy()
+        return lambda feeds: bracketing.pairwise(v)
+
+    @property
+    def cpu_feeds(self):
+        return {}
+
+
+WORKLOADS = {"mlp": MlpWorkload, "cone": ConeWorkload, "int8": Int8Workload, "longsum": LongSumWorkload}
+
+
+# ----------------------------------------------------------------------------- cpu baseline
+
+
+def cpu_baseline(wl, budget_s: float) -> dict:
+    """The oracle's restatement of tgc's CPU path, timed on the host cores."""
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    prog = wl.cpu_program()
+    feeds = wl.cpu_feeds
+    prog(feeds)
+    times = []
+    start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        prog(feeds)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - start > budget_s or len(times) >= 50:
+            break
+    med = statistics.median(times)
+    what = (
+        "oracle/bracketing.c's restatement of tgc's summation.pairwise (1 thread)"
+        if wl.name == "longsum"
+        else "oracle/interp.py (tgc's generated-Python executor restated: one torch CPU op per node into one arena)"
+    )
+    return {
+        "value": 1.0 / med,
+        "unit": wl.unit,
+        "cores": 1 if wl.name == "longsum" else torch.get_num_threads(),
+        "kind": "port",
+        "sample": f"{len(times)} full executions of the same workload by {what}; median {med:.4f} s",
+    }
+
+
+# ----------------------------------------------------------------------------- main
+
+
+def read_traffic(workload: str, kernel_kind: str):
+    """DRAM bytes per launch of the dominant kernel, from the committed ncu summary."""
+    path = os.path.join(REPO, "profiles", "ncu_traffic.txt")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        for line in f:
+            parts = line.split()
+            if len(parts) >= 3 and not line.startswith("#") and parts[0] == workload and parts[1] == kernel_kind:
+                return int(parts[2])
+    return None
+
+
+def main() -> int:
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    n = max(world, 1)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        return run_reference(args, n)
+
+    import torch
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist_mod
+
+        dist_mod.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+        dist = dist_mod
+
+    wl = WORKLOADS[args.workload](rank)
+    wl.setup(device)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    flush_read = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    flush_sink = torch.empty((), dtype=torch.float32, device=device)
+
+    def flush_l2():
+        flush.zero_()
+        torch.sum(flush_read, dim=0, out=flush_sink)
+
+    from tgcb.runtime import delay
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    warm = max(args.warmup, 3)
+    for _ in range(warm):
+        wl.step_profiled()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    sampler.mark_start()
+    per_launch = None
+    step_ms = []
+    for _ in range(args.steps):
+        flush_l2()
+        delay(50_000)
+        ms = wl.step_profiled()
+        step_ms.append(sum(ms))
+        per_launch = ms if per_launch is None else [a + b for a, b in zip(per_launch, ms, strict=True)]
+    torch.cuda.synchronize()
+    sampler.mark_end()
+    clocks = sampler.stop()
+    if hasattr(wl, "compiled"):
+        wl.compiled.check_status()
+    total_ms = sum(step_ms)
+    if dist:
+        dist.barrier()
+        t = torch.tensor([total_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+
+    # end to end through the public API with host buffers
+    for _ in range(2):
+        wl.step_e2e()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e2e_ms = 0.0
+    stream = torch.cuda.current_stream()
+    for _ in range(args.steps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        wl.step_e2e()
+        e.record(stream)
+        e.synchronize()
+        e2e_ms += s.elapsed_time(e)
+    if dist:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+        dist.barrier()
+
+    result = None
+    if rank == 0:
+        pk, src = peaks()
+        work = wl.kernel_work()
+        shares = [p / sum(per_launch) for p in per_launch]
+        dom = max(range(len(per_launch)), key=lambda i: per_launch[i])
+        dk = work[dom]
+        avg_ms = per_launch[dom] / args.steps
+        if dk["bound"] == "tensor":
+            factor = 0.5 if dk.get("type") == "tf32" else 2.0
+            peak = pk["bf16_tflops_sustained"] * factor
+            achieved = dk["work"] / (avg_ms * 1e-3) / 1e12
+            unit = "TFLOP/s" if dk.get("type") == "tf32" else "TOP/s"
+            peak_note = (
+                f"{'tf32' if factor == 0.5 else 'int8'} dense rate taken as {factor}x the {src} sustained bf16 "
+                f"cuBLAS rate ({pk['bf16_tflops_sustained']} TF/s, MEASURED_PEAKS.json); B200 dense tf32:bf16:int8 = 1:2:4"
+            )
+        else:
+            peak = pk["hbm_gbs"]
+            achieved = dk["work"] / (avg_ms * 1e-3) / 1e9
+            unit = "GB/s"
+            peak_note = f"{src} STREAM-style copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"
+        value = n * args.steps / (total_ms * 1e-3)
+        hbm_bytes = sum(w["work"] for w in work if w["bound"] == "hbm")
+        hbm_ms = sum(per_launch[i] for i, w in enumerate(work) if w["bound"] == "hbm") / args.steps
+        result = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": wl.unit,
+            "n_gpus": n,
+            "steps": args.steps,
+            "warmup": warm,
+            "ms_per_step": round(total_ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": wl.dtype,
+            "data": "synthetic: seeded torch.randn inputs and random-init weights of the workload's shapes",
+            "config": {**wl.config(), "parallelism": f"dp{n}: independent row shards per GPU, no collective"},
+            "roofline": {
+                "bound": dk["bound"],
+                "kernel": dk["name"],
+                "achieved": round(achieved, 2),
+                "peak": round(peak, 1),
+                "unit": unit,
+                "frac": round(achieved / peak, 4),
+                "traffic": read_traffic(args.workload, dk["kind"]),
+                "peak_source": peak_note,
+            },
+            "hbm_kernels": {
+                "algorithmic_bytes_per_exec": hbm_bytes,
+                "achieved_gbs": round(hbm_bytes / (hbm_ms * 1e-3) / 1e9, 1) if hbm_ms > 0 else None,
+                "frac_of_measured_hbm": round(hbm_bytes / (hbm_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4) if hbm_ms > 0 else None,
+            },
+            "kernels": [
+                {"name": w["name"], "kind": w["kind"], "avg_ms": round(per_launch[i] / args.steps, 4), "share": round(shares[i], 4)}
+                for i, w in enumerate(work)
+            ],
+            "e2e": {
+                "value": round(n * args.steps / (e2e_ms * 1e-3), 3),
+                "unit": wl.unit,
+                "h2d_bytes_per_step": wl.h2d_bytes(),
+                "d2h_bytes_per_step": wl.d2h_bytes(),
+            },
+            "gpu_launches": args.steps * wl.launches_per_step(),
+            "clocks": clocks,
+        }
+        if n == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+    return 0
+
+
+def run_reference(args, n: int) -> int:
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    wl = WORKLOADS[args.workload](0)
+    if args.workload == "longsum":
+        from tgcb import workloads
+
+        wl.v, _ = workloads.longsum_input(wl.n)
+    else:
+        wl.g = wl.graph()
+        wl.cpu_feeds = wl.feeds()
+    prog = wl.cpu_program()
+    feeds = wl.cpu_feeds
+    warm = max(1, min(args.warmup, 2))
+    for _ in range(warm):
+        prog(feeds)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        prog(feeds)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = args.steps / total
+    cores = 1 if args.workload == "longsum" else torch.get_num_threads()
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": wl.unit,
+        "n_gpus": n,
+        "steps": args.steps,
+        "warmup": warm,
+        "ms_per_step": round(total / args.steps * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: seeded torch.randn inputs and random-init weights of the workload's shapes",
+        "config": {**wl.config(), "parallelism": "host CPU, rank 0 only"},
+        "cpu_baseline": {
+            "value": round(value, 4),
+            "unit": wl.unit,
+            "cores": cores,
+            "kind": "port",
+            "sample": "each step one full execution of the workload by oracle/ (tgc's CPU path restated; "
+            "tgc's own source is not present on the GPU hosts)",
+        },
+        "e2e": {"value": round(value, 4), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -112,6 +112,18 @@ int tgcb_plan_run(tgcb_plan* p, void* arena, const void* const* inputs, int n_in
 /* Number of launches a plan queues per run. */
 int tgcb_plan_launch_count(const tgcb_plan* p);
 
+/* tgcb_plan_run with a CUDA event recorded on `stream` before the first launch and after
+ * every launch; waits for the stream and writes each launch's device time in milliseconds to
+ * ms[0 .. launch_count). The measurement tgc's runtime/profile.py:91-145 takes with
+ * perf_counter around the whole call, taken per kernel on the device instead. */
+int tgcb_plan_run_profiled(tgcb_plan* p, void* arena, const void* const* inputs, int n_inputs, void* stream,
+                           float* ms);
+
+/* Queue a kernel on `stream` that spins for about `ns` nanoseconds (capped at 10 ms) and
+ * exits. Benchmarks put it before a timed region so the launches behind it start back to
+ * back instead of waiting on the host. */
+int tgcb_delay(uint64_t ns, void* stream);
+
 /* Read (and with clear != 0, reset) the device status word of the current device.
  * Synchronises the device. *status = 0 means every kernel so far completed normally. */
 int tgcb_status(int clear, int* status);

@@ -170,6 +170,22 @@ def relative_difference(left, right) -> float:
     return largest_difference(left, right) / scale
 
 
+def generated_python_program(graph):
+    """tgc's compile path on the CPU: exact pipeline, depth-first order, liveness over nodes,
+    largest-first plan, then the arena program (executor.py:91-122). Uses tgcb's restatements
+    of tgc's pipeline and planner, which the golden tests pin to tgc's printed graphs."""
+    from tgcb import memory, passes
+
+    opt, _ = passes.default_pipeline().run(graph)
+    order = memory.depth_first_order(opt)
+    sizes = {v.name: v.bytes for v in opt.inputs}
+    sizes.update({n.output.name: n.output.bytes for n in opt.nodes})
+    steps = [(list(n.inputs), [n.output.name]) for n in order]
+    intervals = memory.intervals_for_steps([v.name for v in opt.inputs], steps, list(opt.outputs), sizes)
+    plan = memory.plan_largest_first(intervals)
+    return ArenaProgram(opt, order, {a.name: a.offset for a in plan.allocations}, plan.arena_bytes)
+
+
 class ArenaProgram:
     """tgc's generated-Python execution (emit.py:92-209, executor.py:52-79) on the CPU.
 

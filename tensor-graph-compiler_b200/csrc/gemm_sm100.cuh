@@ -32,7 +32,12 @@ constexpr int B_STAGE = BN * ROW_BYTES;   // 32 KB
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 2 * BN;
-constexpr int SMEM_BYTES = STAGES * (A_STAGE + B_STAGE) + 1024 + 256;
+constexpr int BAR_BYTES = 256;
+// Each epilogue warp transposes 32 rows x 16 columns through shared memory (row pitch 17
+// words: conflict-free writes of a row per lane and reads of a column per lane).
+constexpr int STAGE_PITCH = 17;
+constexpr int EPI_STAGE_BYTES = EPI_WARPS * 32 * STAGE_PITCH * 4;
+constexpr int SMEM_BYTES = STAGES * (A_STAGE + B_STAGE) + BAR_BYTES + EPI_STAGE_BYTES + 1024;
 constexpr unsigned long long WAIT_BUDGET_NS = 4000000000ull;  // 4 s
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -285,6 +290,7 @@ __device__ __forceinline__ void gemm_body(const TgcbArgs& args, const TgcbTmaDes
     const int ew = warp - 2;
     const int quad = warp & 3;
     const int half = ew >> 2;  // which half of the 256 columns this warp drains
+    uint32_t* stage = reinterpret_cast<uint32_t*>(smem + STAGES * (A_STAGE + B_STAGE) + BAR_BYTES) + ew * 32 * STAGE_PITCH;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < NUM_TILES; tile += gridDim.x) {
@@ -295,22 +301,29 @@ __device__ __forceinline__ void gemm_body(const TgcbArgs& args, const TgcbTmaDes
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
       tc_fence_after();
-      const long long row = (long long)tm * BM + quad * 32 + lane;
+      const long long row0 = (long long)tm * BM + quad * 32;
 #pragma unroll 1
       for (int chunk = half * (BN / 32); chunk < (half + 1) * (BN / 32); ++chunk) {
         uint32_t r[16];
         tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + chunk * 16), r);
-        if constexpr (INT8) {
-          int v[16];
+        // lane = row on the way in; lanes run along columns on the way out, so the
+        // epilogue's side-input loads and its stores are coalesced along the row.
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = (int)r[j];
-          Epi::apply(args, row, (long long)tn * BN + chunk * 16, v);
-        } else {
-          float v[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-          Epi::apply(args, row, (long long)tn * BN + chunk * 16, v);
+        for (int j = 0; j < 16; ++j) stage[lane * STAGE_PITCH + j] = r[j];
+        __syncwarp();
+        const long long col0 = (long long)tn * BN + chunk * 16;
+#pragma unroll 4
+        for (int it = 0; it < 16; ++it) {
+          const int rr = 2 * it + (lane >> 4);
+          const int cc = lane & 15;
+          const uint32_t bits = stage[rr * STAGE_PITCH + cc];
+          if constexpr (INT8) {
+            Epi::apply(args, row0 + rr, col0 + cc, (int)bits);
+          } else {
+            Epi::apply(args, row0 + rr, col0 + cc, __uint_as_float(bits));
+          }
         }
+        __syncwarp();
       }
       tc_fence_before();
       __syncwarp();

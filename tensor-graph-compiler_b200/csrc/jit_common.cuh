@@ -87,6 +87,34 @@ __device__ __forceinline__ T tgcb_tree_combine_max(const T* p) {
   return v[0];
 }
 
+// Reductions over one row handled by the W warps of a row group (W = threads per row / 32).
+// `tid` is the thread's index within its row group; `smem` holds W slots for this group.
+// Every thread of the CTA must call these the same number of times (the row groups of a
+// CTA run in lockstep), since W > 1 uses __syncthreads.
+template <typename T, int W>
+__device__ __forceinline__ T tgcb_group_sum(T v, T* smem, int tid) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) v = v + tgcb_shfl_xor(v, o);
+  if (W == 1) return v;
+  if ((tid & 31) == 0) smem[tid >> 5] = v;
+  __syncthreads();
+  T r = tgcb_tree_combine_sum<T, W>(smem);
+  __syncthreads();
+  return r;
+}
+
+template <typename T, int W>
+__device__ __forceinline__ T tgcb_group_max(T v, T* smem, int tid) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) v = tgcb_nanmax(v, tgcb_shfl_xor(v, o));
+  if (W == 1) return v;
+  if ((tid & 31) == 0) smem[tid >> 5] = v;
+  __syncthreads();
+  T r = tgcb_tree_combine_max<T, W>(smem);
+  __syncthreads();
+  return r;
+}
+
 template <typename T, int W>
 __device__ __forceinline__ T tgcb_block_sum(T v, T* smem) {
 #pragma unroll

@@ -254,53 +254,134 @@ static int encode_operand(DeviceState* st, const tgcb_operand_desc& od, const vo
   return TGCB_OK;
 }
 
-int tgcb_plan_run(tgcb_plan* p, void* arena, const void* const* inputs, int n_inputs, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Argument checks and the TgcbArgs block shared by every launch of one plan run.
+int prepare_run(tgcb_plan* p, void* arena, const void* const* inputs, int n_inputs, DeviceState** st, TgcbArgs* args) {
   if (p == nullptr) return fail(TGCB_E_INVALID, "tgcb_plan_run: null plan");
   if (n_inputs < 0 || n_inputs > TGCB_MAX_INPUTS)
     return fail(TGCB_E_INVALID, "a plan takes at most %d inputs, got %d", TGCB_MAX_INPUTS, n_inputs);
   if (p->arena_bytes > 0 && arena == nullptr) return fail(TGCB_E_INVALID, "tgcb_plan_run: null arena");
   if ((reinterpret_cast<uintptr_t>(arena) & 255u) != 0) return fail(TGCB_E_INVALID, "the arena is not 256-byte aligned");
-  DeviceState* st = nullptr;
-  int rc = current_state(&st);
+  int rc = current_state(st);
   if (rc != TGCB_OK) return rc;
+  memset(args, 0, sizeof(*args));
+  args->arena = static_cast<char*>(arena);
+  for (int i = 0; i < n_inputs; ++i) args->in[i] = static_cast<const char*>(inputs[i]);
+  args->status = (*st)->status;
+  return TGCB_OK;
+}
+
+// Queue one launch; GEMM tensor maps are re-encoded only when an operand address changed.
+int launch_one(DeviceState* st, LaunchState& ls, TgcbArgs& args, void* arena, const void* const* inputs, int n_inputs,
+               cudaStream_t s) {
+  const tgcb_launch_desc& d = ls.desc;
+  dim3 grid(d.grid[0], d.grid[1], d.grid[2]);
+  dim3 block(d.block[0], d.block[1], d.block[2]);
+  cudaError_t e;
+  if (d.is_gemm) {
+    const tgcb_operand_desc* ods[2] = {&d.a, &d.b};
+    const void** cached[2] = {&ls.a_ptr, &ls.b_ptr};
+    CUtensorMap* maps[2] = {&ls.ta, &ls.tb};
+    for (int k = 0; k < 2; ++k) {
+      const tgcb_operand_desc& od = *ods[k];
+      const void* base;
+      if (od.input_index >= 0) {
+        if (od.input_index >= n_inputs) return fail(TGCB_E_INVALID, "GEMM operand reads missing input %d", od.input_index);
+        base = inputs[od.input_index];
+      } else {
+        base = static_cast<const char*>(arena) + od.arena_offset;
+      }
+      if (base != *cached[k]) {
+        int rc = encode_operand(st, od, base, maps[k]);
+        if (rc != TGCB_OK) return rc;
+        *cached[k] = base;
+      }
+    }
+    void* params[3] = {&args, &ls.ta, &ls.tb};
+    e = cudaLaunchKernel(reinterpret_cast<const void*>(ls.kernel), grid, block, params, d.smem_bytes, s);
+  } else {
+    void* params[1] = {&args};
+    e = cudaLaunchKernel(reinterpret_cast<const void*>(ls.kernel), grid, block, params, d.smem_bytes, s);
+  }
+  if (e != cudaSuccess) return fail(TGCB_E_CUDA, "launching %s: %s", d.kernel, cudaGetErrorString(e));
+  return TGCB_OK;
+}
+
+__global__ void delay_kernel(unsigned long long ns) {
+  unsigned long long start;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(start));
+  for (int i = 0; i < (1 << 22); ++i) {  // bounded: at most ~4M polls
+    unsigned long long now;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+    if (now - start >= ns) break;
+    __nanosleep(1000);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int tgcb_plan_run(tgcb_plan* p, void* arena, const void* const* inputs, int n_inputs, void* stream) {
+  DeviceState* st = nullptr;
   TgcbArgs args;
-  memset(&args, 0, sizeof(args));
-  args.arena = static_cast<char*>(arena);
-  for (int i = 0; i < n_inputs; ++i) args.in[i] = static_cast<const char*>(inputs[i]);
-  args.status = st->status;
+  int rc = prepare_run(p, arena, inputs, n_inputs, &st, &args);
+  if (rc != TGCB_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   for (LaunchState& ls : p->launches) {
-    const tgcb_launch_desc& d = ls.desc;
-    dim3 grid(d.grid[0], d.grid[1], d.grid[2]);
-    dim3 block(d.block[0], d.block[1], d.block[2]);
-    cudaError_t e;
-    if (d.is_gemm) {
-      const tgcb_operand_desc* ods[2] = {&d.a, &d.b};
-      const void** cached[2] = {&ls.a_ptr, &ls.b_ptr};
-      CUtensorMap* maps[2] = {&ls.ta, &ls.tb};
-      for (int k = 0; k < 2; ++k) {
-        const tgcb_operand_desc& od = *ods[k];
-        const void* base;
-        if (od.input_index >= 0) {
-          if (od.input_index >= n_inputs) return fail(TGCB_E_INVALID, "GEMM operand reads missing input %d", od.input_index);
-          base = inputs[od.input_index];
-        } else {
-          base = static_cast<const char*>(arena) + od.arena_offset;
-        }
-        if (base != *cached[k]) {
-          rc = encode_operand(st, od, base, maps[k]);
-          if (rc != TGCB_OK) return rc;
-          *cached[k] = base;
-        }
-      }
-      void* params[3] = {&args, &ls.ta, &ls.tb};
-      e = cudaLaunchKernel(reinterpret_cast<const void*>(ls.kernel), grid, block, params, d.smem_bytes, s);
-    } else {
-      void* params[1] = {&args};
-      e = cudaLaunchKernel(reinterpret_cast<const void*>(ls.kernel), grid, block, params, d.smem_bytes, s);
-    }
-    if (e != cudaSuccess) return fail(TGCB_E_CUDA, "launching %s: %s", d.kernel, cudaGetErrorString(e));
+    rc = launch_one(st, ls, args, arena, inputs, n_inputs, s);
+    if (rc != TGCB_OK) return rc;
   }
+  return TGCB_OK;
+}
+
+int tgcb_plan_run_profiled(tgcb_plan* p, void* arena, const void* const* inputs, int n_inputs, void* stream,
+                           float* ms) {
+  if (ms == nullptr) return fail(TGCB_E_INVALID, "tgcb_plan_run_profiled: null output");
+  DeviceState* st = nullptr;
+  TgcbArgs args;
+  int rc = prepare_run(p, arena, inputs, n_inputs, &st, &args);
+  if (rc != TGCB_OK) return rc;
+  const size_t n = p->launches.size();
+  std::vector<cudaEvent_t> ev(n + 1, nullptr);
+  for (auto& e : ev) {
+    cudaError_t err = cudaEventCreate(&e);
+    if (err != cudaSuccess) {
+      rc = fail(TGCB_E_CUDA, "cudaEventCreate: %s", cudaGetErrorString(err));
+      break;
+    }
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (rc == TGCB_OK) {
+    cudaError_t err = cudaEventRecord(ev[0], s);
+    if (err != cudaSuccess) rc = fail(TGCB_E_CUDA, "cudaEventRecord: %s", cudaGetErrorString(err));
+  }
+  for (size_t i = 0; i < n && rc == TGCB_OK; ++i) {
+    rc = launch_one(st, p->launches[i], args, arena, inputs, n_inputs, s);
+    if (rc != TGCB_OK) break;
+    cudaError_t err = cudaEventRecord(ev[i + 1], s);
+    if (err != cudaSuccess) rc = fail(TGCB_E_CUDA, "cudaEventRecord: %s", cudaGetErrorString(err));
+  }
+  if (rc == TGCB_OK) {
+    cudaError_t err = cudaStreamSynchronize(s);
+    if (err != cudaSuccess) rc = fail(TGCB_E_CUDA, "cudaStreamSynchronize: %s", cudaGetErrorString(err));
+  }
+  for (size_t i = 0; i < n && rc == TGCB_OK; ++i) {
+    cudaError_t err = cudaEventElapsedTime(&ms[i], ev[i], ev[i + 1]);
+    if (err != cudaSuccess) rc = fail(TGCB_E_CUDA, "cudaEventElapsedTime: %s", cudaGetErrorString(err));
+  }
+  for (auto& e : ev)
+    if (e) cudaEventDestroy(e);
+  return rc;
+}
+
+int tgcb_delay(uint64_t ns, void* stream) {
+  if (ns > 10000000ull) ns = 10000000ull;
+  delay_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(ns);
+  CUDA_TRY(cudaGetLastError());
   return TGCB_OK;
 }
 

@@ -83,6 +83,11 @@ SIGNATURES = {
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_void_p],
     ),
     "tgcb_plan_launch_count": (ctypes.c_int, [ctypes.c_void_p]),
+    "tgcb_plan_run_profiled": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_float)],
+    ),
+    "tgcb_delay": (ctypes.c_int, [ctypes.c_uint64, ctypes.c_void_p]),
     "tgcb_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "tgcb_sum_pairwise_scratch_bytes": (ctypes.c_size_t, [ctypes.c_uint64, ctypes.c_int]),
     "tgcb_sum_pairwise_f32": (

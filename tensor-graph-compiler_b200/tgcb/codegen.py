@@ -97,8 +97,13 @@ def _next_pow2(x: int) -> int:
 
 
 def row_threads(cols: int) -> int:
-    """Threads per row in a row kernel: a power of two in [32, 256], about 4 columns each."""
-    return max(32, min(256, _next_pow2(max(1, (cols + 3) // 4))))
+    """Threads per row in a row kernel: a power of two in [32, 256] giving each thread at most
+    32 columns (a single warp per row up to 1024 columns), so a thread keeps up to 32
+    independent loads in flight and reductions of short rows need no block barrier."""
+    return max(32, min(256, _next_pow2(max(1, (cols + 31) // 32))))
+
+
+ROW_BLOCK = 256  # threads per CTA of a row kernel; 256 // T rows are processed side by side
 
 
 class Lowering:
@@ -506,9 +511,10 @@ class Lowering:
             return None
 
         shared_eb = ExprBuilder(self.values, self.producers, self._pointer_of, member_resolve, indent="    ")
+        RPB = ROW_BLOCK // T  # rows side by side in one CTA, T threads each
 
         def col_expr(k):
-            return f"((long long)threadIdx.x + {k * T}LL)" if unrolled else "col"
+            return f"((long long)tid + {k * T}LL)" if unrolled else "col"
 
         for phase in range(1, max_phase + 1):
             pm = [m for m in members if group.phase[m] == phase]
@@ -516,12 +522,11 @@ class Lowering:
             for m in pm:
                 node = self.producers[m]
                 t = ctype(node.output.dtype)
-                src_t = ctype(self.values[node.inputs[0]].dtype)
                 if node.op.name == "max":
                     init = "-INFINITY" if t in ("float", "double") else ("(-2147483647-1)" if t == "int" else "(-9223372036854775807LL-1)")
                 else:
                     init = f"({t})0"
-                accs[m] = (f"acc_{slot[m]}", t, node.op.name, src_t)
+                accs[m] = (f"acc_{slot[m]}", t, node.op.name)
                 lines.append(f"    {t} acc_{slot[m]} = {init};")
             if unrolled:
                 eb = shared_eb
@@ -529,14 +534,14 @@ class Lowering:
             else:
                 eb = ExprBuilder(self.values, self.producers, self._pointer_of, member_resolve, indent="      ")
                 ks = [0]
-                lines.append(f"    for (long long col = threadIdx.x; col < {C}LL; col += {T}LL) {{")
+                lines.append(f"    for (long long col = tid; col < {C}LL; col += {T}LL) {{")
             for k in ks:
                 col = col_expr(k)
                 colc = f"tgcb_min_ll({col}, {C - 1}LL)" if (unrolled and C % T) else col
                 for m in pm:
                     node = self.producers[m]
                     v = eb.value(node.inputs[0], row_idx + (colc,))
-                    acc, t, opn, _ = accs[m]
+                    acc, t, opn = accs[m]
                     if opn == "max":
                         upd = f"(({acc}) != ({acc}) || ({acc}) > ({v})) ? ({acc}) : ({t})({v})"
                     else:
@@ -549,14 +554,13 @@ class Lowering:
             if not unrolled:
                 lines.extend(eb.lines)
                 lines.append("    }")
-            # block-level combine of this phase's accumulators, declared tree bracketing
+            # combine the row's partials with the declared tree bracketing
             for m in pm:
-                acc, t, opn, _ = accs[m]
-                fn = "tgcb_block_max" if opn == "max" else "tgcb_block_sum"
-                lines.append(f"    {t} red_{slot[m]} = {fn}<{t}, {W}>({acc}, reinterpret_cast<{t}*>(red_smem[{slot[m]}]));")
+                acc, t, opn = accs[m]
+                fn = "tgcb_group_max" if opn == "max" else "tgcb_group_sum"
+                lines.append(f"    {t} red_{slot[m]} = {fn}<{t}, {W}>({acc}, reinterpret_cast<{t}*>(red_smem[{slot[m]}][grp]), tid);")
                 if opn == "mean":
                     lines.append(f"    red_{slot[m]} = red_{slot[m]} / ({t}){C};")
-            lines.append("    __syncthreads();")
         # final phase: full-shaped requests
         if full_req:
             if unrolled:
@@ -567,22 +571,22 @@ class Lowering:
                     for r in full_req:
                         v = eb.value(r, row_idx + (colc,))
                         st = f"reinterpret_cast<{ctype(self.values[r].dtype)}*>({PTR(r)})[row * {C}LL + {col}] = {v};"
-                        eb.emit(f"if ({col} < {C}LL) {st}" if C % T else st)
+                        eb.emit(f"if (live && {col} < {C}LL) {st}" if C % T else f"if (live) {st}")
                     lines.extend(eb.lines)
                     eb.lines = []
             else:
                 eb = ExprBuilder(self.values, self.producers, self._pointer_of, member_resolve, indent="      ")
-                lines.append(f"    for (long long col = threadIdx.x; col < {C}LL; col += {T}LL) {{")
+                lines.append(f"    for (long long col = tid; col < {C}LL; col += {T}LL) {{")
                 for r in full_req:
                     v = eb.value(r, row_idx + ("col",))
-                    eb.emit(f"reinterpret_cast<{ctype(self.values[r].dtype)}*>({PTR(r)})[row * {C}LL + col] = {v};")
+                    eb.emit(f"if (live) reinterpret_cast<{ctype(self.values[r].dtype)}*>({PTR(r)})[row * {C}LL + col] = {v};")
                 lines.extend(eb.lines)
                 lines.append("    }")
         # per-row results: materialised reductions and row-shaped requests
         row_stores = [m for m in members if m in self.materialised] + row_req
         if row_stores:
             eb = ExprBuilder(self.values, self.producers, self._pointer_of, member_resolve, indent="      ")
-            lines.append("    if (threadIdx.x == 0) {")
+            lines.append("    if (tid == 0 && live) {")
             for r in row_stores:
                 rs = self.sizes(r)
                 idx = row_idx + ("0",) if len(rs) == len(ss) else row_idx
@@ -590,12 +594,19 @@ class Lowering:
                 eb.emit(f"reinterpret_cast<{ctype(self.values[r].dtype)}*>({PTR(r)})[row] = {v};")
             lines.extend(eb.lines)
             lines.append("    }")
+        if W > 1:
+            lines.append("    __syncthreads();")
         reads |= shared_eb.loads
-        grid = max(1, min(R, NUM_SMS * max(1, 2048 // T) * 2))
+        row_blocks = (R + RPB - 1) // RPB
+        grid = max(1, min(row_blocks, NUM_SMS * (2048 // ROW_BLOCK) * 2))
         src = (
-            f'extern "C" __global__ void __launch_bounds__({T}) {kname}(const TgcbArgs args) {{\n'
-            f"  __shared__ double red_smem[{nred}][{W}];\n"
-            f"  for (long long row = blockIdx.x; row < {R}LL; row += gridDim.x) {{\n"
+            f'extern "C" __global__ void __launch_bounds__({ROW_BLOCK}) {kname}(const TgcbArgs args) {{\n'
+            f"  __shared__ double red_smem[{nred}][{RPB}][{W}];\n"
+            f"  const int tid = threadIdx.x % {T};\n"
+            f"  const int grp = threadIdx.x / {T};\n"
+            f"  for (long long rb = (long long)blockIdx.x * {RPB}; rb < {R}LL; rb += (long long)gridDim.x * {RPB}) {{\n"
+            f"    const bool live = rb + grp < {R}LL;\n"
+            f"    const long long row = live ? rb + grp : {R - 1}LL;\n"
             + "\n".join(lines)
             + "\n  }\n}\n"
         )
@@ -614,8 +625,8 @@ class Lowering:
             reads=sorted(reads),
             writes=writes,
             source=src,
-            launches=[Launch(kname, (grid, 1, 1), (T, 1, 1))],
-            bracketing=f"row tree: {T} threads, thread t sums columns t, t+{T}, ... in order; "
+            launches=[Launch(kname, (grid, 1, 1), (ROW_BLOCK, 1, 1))],
+            bracketing=f"row tree: {T} threads per row, thread t sums columns t, t+{T}, ... in order; "
             f"lanes combined by xor tree (1,2,4,8,16); {W} warp partials combined as a balanced tree",
             nodes=list(members) + list(requests),
         )
@@ -814,31 +825,25 @@ class Lowering:
             stores.insert(0, name)
         kname = self._kname("gemm")
         acc_t = "int" if is_int else "float"
-        chunk = 16
 
-        lines = []
-        for j in range(chunk):
-            col = f"(col0 + {j})"
+        # The epilogue runs once per output element (row, col) with the accumulator value;
+        # the kernel calls it with consecutive lanes on consecutive columns, so every load of
+        # a side input and every store below is coalesced along the row.
+        def resolve(n, idx):
+            if n == name:
+                return "acc"
+            return None
 
-            def resolve(n, idx, col=col):
-                if n == name:
-                    return f"acc[{j}]"
-                return None
-
-            eb = ExprBuilder(self.values, self.producers, self._pointer_of, resolve, indent="      ")
-            st = []
-            for r in stores:
-                v = eb.value(r, ("row", col))
-                st.append(f"      reinterpret_cast<{ctype(self.values[r].dtype)}*>({PTR(r)})[row * {N}LL + {col}] = {v};")
-            lines.append(f"    if ({col} < {N}LL) {{")
-            lines.extend(eb.lines)
-            lines.extend(st)
-            lines.append("    }")
+        eb = ExprBuilder(self.values, self.producers, self._pointer_of, resolve, indent="    ")
+        st = []
+        for r in stores:
+            v = eb.value(r, ("row", "col"))
+            st.append(f"    reinterpret_cast<{ctype(self.values[r].dtype)}*>({PTR(r)})[row * {N}LL + col] = {v};")
         epi_name = f"Epi_{kname}"
         epi = (
             f"struct {epi_name} {{\n"
-            f"  static __device__ __forceinline__ void apply(const TgcbArgs& args, long long row, long long col0, const {acc_t} (&acc)[{chunk}]) {{\n"
-            f"    if (row >= {M}LL) return;\n" + "\n".join(lines) + "\n  }\n};\n"
+            f"  static __device__ __forceinline__ void apply(const TgcbArgs& args, long long row, long long col, const {acc_t} acc) {{\n"
+            f"    if (row >= {M}LL || col >= {N}LL) return;\n" + "\n".join(eb.lines + st) + "\n  }\n};\n"
         )
         reads = {a_base, b_base}
         for r in requests:
@@ -900,7 +905,7 @@ class Lowering:
             f"    for (int j = 0; j < 16; ++j) {{\n"
             f"      if (col0 + j < {N}LL) {{ const {at} b = {load_b}; {fma} }}\n"
             f"    }}\n  }}\n"
-            f"  {epi_name}::apply(args, row, col0, acc);\n}}\n"
+            f"  for (int j = 0; j < 16; ++j) {epi_name}::apply(args, row, col0 + j, acc[j]);\n}}\n"
         )
 
 

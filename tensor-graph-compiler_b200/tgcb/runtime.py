@@ -41,7 +41,9 @@ SUPPORTED_OPS = {
     "sigmoid", "reciprocal", "abs", "step", "cast", "matmul", "sum", "mean", "max", "reshape",
     "transpose", "broadcast_to", "concat", "slice", "constant", "print", "assert_finite",
 }
-GEMM_SMEM = 4 * (128 + 256) * 128 + 1024 + 256
+# tgcb_gemm::SMEM_BYTES: 4 stages of (128 + 256) rows x 128 B, barriers, the epilogue
+# transpose tiles (8 warps x 32 x 17 words) and 1 KB of alignment slack.
+GEMM_SMEM = 4 * (128 + 256) * 128 + 256 + 8 * 32 * 17 * 4 + 1024
 _PLACEHOLDER = re.compile(r"@P<([^>]+)>@")
 
 TORCH_DTYPES = {}
@@ -354,14 +356,35 @@ class CompiledGraph:
             arr = (ctypes.c_void_p * max(1, len(ptrs)))(*ptrs)
             rc = _lib.load().tgcb_plan_run(self._plan, ctypes.c_void_p(arena.data_ptr()), arr, len(ptrs), ctypes.c_void_p(s.cuda_stream))
             _lib.check(rc, "running the compiled graph")
-            outs = []
-            for name, shape, dtype, nbytes in self._out_specs:
-                if name in self.input_names:
-                    outs.append(feeds[name].to(device=arena.device, dtype=dtype).clone())
-                    continue
-                off = self.module.offsets[name]
-                outs.append(arena[off : off + nbytes].view(dtype).view(shape))
-            return outs
+            return self._outputs(arena, feeds)
+
+    def run_profiled(self, arena, feeds: dict, stream=None) -> tuple[list, list[float]]:
+        """Run once with a CUDA event around every launch; returns (outputs, ms per launch).
+
+        Waits for the stream. The events are recorded on the stream the kernels run on.
+        """
+        torch = self._torch
+        with torch.cuda.device(self.device):
+            s = stream if stream is not None else torch.cuda.current_stream(self.device)
+            ptrs = self.input_pointers(arena, feeds)
+            arr = (ctypes.c_void_p * max(1, len(ptrs)))(*ptrs)
+            n = len(self.module.launches)
+            ms = (ctypes.c_float * max(1, n))()
+            rc = _lib.load().tgcb_plan_run_profiled(
+                self._plan, ctypes.c_void_p(arena.data_ptr()), arr, len(ptrs), ctypes.c_void_p(s.cuda_stream), ms
+            )
+            _lib.check(rc, "running the compiled graph (profiled)")
+            return self._outputs(arena, feeds), [float(ms[i]) for i in range(n)]
+
+    def _outputs(self, arena, feeds: dict) -> list:
+        outs = []
+        for name, shape, dtype, nbytes in self._out_specs:
+            if name in self.input_names:
+                outs.append(feeds[name].to(device=arena.device, dtype=dtype).clone())
+                continue
+            off = self.module.offsets[name]
+            outs.append(arena[off : off + nbytes].view(dtype).view(shape))
+        return outs
 
     def check_status(self) -> None:
         """Synchronise and raise ``DeviceError`` if any kernel recorded a device-side failure."""
@@ -389,6 +412,14 @@ def compile_graph(graph, *, pipeline=None, optimise: bool = True, device: int | 
     dev = torch.cuda.current_device() if device is None else device
     optimised, order, plan, module, lowering = generate(graph, pipeline=pipeline, optimise=optimise)
     return CompiledGraph(optimised, order, plan, module, lowering, dev)
+
+
+def delay(ns: int, stream=None) -> None:
+    """Queue a bounded spin kernel (at most 10 ms) so launches queued behind it start back to back."""
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream()
+    _lib.check(_lib.load().tgcb_delay(int(ns), ctypes.c_void_p(s.cuda_stream)), "tgcb_delay")
 
 
 def source_of(graph) -> str:

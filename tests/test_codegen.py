@@ -1,0 +1,124 @@
+"""Lowering: how graphs are partitioned into kernels, planned, and compiled (no GPU needed:
+NVRTC compiles sm_100a code on any host)."""
+
+from __future__ import annotations
+
+import os
+
+import pytest
+from conftest import GOLDEN
+
+from tgcb import ir, memory, runtime, serialize, workloads
+from tgcb.codegen import row_threads
+from tgcb.errors import CodegenError
+
+
+def kinds(graph):
+    return [s.kind for s in runtime.generate(graph)[3].steps]
+
+
+def load_graph(name):
+    with open(os.path.join(GOLDEN, "graphs", f"{name}.tgc")) as f:
+        return serialize.loads(f.read())
+
+
+def test_cone_is_one_row_kernel():
+    _, _, plan, mod, low = runtime.generate(workloads.cone_graph(ir.Builder))
+    assert [s.kind for s in mod.steps] == ["row"]
+    # only x and the three row results touch memory: 16 MiB + 3 x 16 KiB
+    assert mod.arena_bytes == 4096 * 1024 * 4 + 3 * 4096 * 4
+    assert set(mod.steps[0].writes) == set(low.outputs)
+
+
+def test_mlp_is_layernorm_then_two_gemms():
+    _, _, plan, mod, low = runtime.generate(workloads.mlp_graph(ir.Builder))
+    assert [s.kind for s in mod.steps] == ["row", "gemm", "gemm"]
+    ln, g1, g2 = mod.steps
+    assert len(ln.writes) == 1  # the normalised x, read by the first GEMM
+    assert "tanhf" in g1.source  # GELU fused into the first GEMM's epilogue
+    assert "tgcb_gemm::gemm_body<8192, 4096, 1024, false, false, true" in g1.source
+    assert "tgcb_gemm::gemm_body<8192, 1024, 4096, false, false, true" in g2.source
+
+
+def test_int8_linear_is_one_int8_gemm_with_fused_dequant():
+    mod = runtime.generate(workloads.int8_linear_graph(ir.Builder, ir.INT8, ir.INT32, ir.FLOAT32))[3]
+    assert [s.kind for s in mod.steps] == ["gemm"]
+    # int8 operands read directly, both K-major (the weight arrives transposed)
+    assert "gemm_body<8192, 4096, 4096, true, false, false" in mod.steps[0].source
+    assert len(mod.steps[0].writes) == 2  # the int32 accumulator and the dequantised output
+
+
+def test_gradient_graph_lowers():
+    g = load_graph("train_grad_8192")
+    mod = runtime.generate(g)[3]
+    ks = [s.kind for s in mod.steps]
+    assert ks.count("gemm") == 5
+    assert ks.count("colreduce") == 2
+    # transposes are absorbed as operand majors, never materialised
+    assert all("transpose" not in s.kind for s in mod.steps)
+
+
+@pytest.mark.parametrize("cols,expect", [(1, 32), (1024, 32), (1025, 64), (4096, 128), (8192, 256), (20000, 256)])
+def test_row_threads(cols, expect):
+    assert row_threads(cols) == expect
+
+
+def test_plans_keep_live_values_apart():
+    for g in (workloads.mlp_graph(ir.Builder, rows=512), load_graph("train_grad_small"), load_graph("fixture_softmax_graph")):
+        og, order, plan, mod, low = runtime.generate(g)
+        sizes = {v.name: v.bytes for v in og.inputs}
+        for s in mod.steps:
+            for w in s.writes:
+                sizes[w] = low.scratch.get(w, low.values[w].bytes if w in low.values else 0)
+        iv = memory.intervals_for_steps(low.inputs, [(s.reads, s.writes) for s in mod.steps], low.outputs, sizes)
+        memory.validate_plan(iv, plan)
+
+
+@pytest.mark.parametrize(
+    "name",
+    ["cone", "mlp", "int8", "grad_small", "fixture_softmax_graph", "fixture_layernorm_graph", "fixture_diamond_graph",
+     "fixture_branching_graph", "fixture_mlp_graph", "sum"],
+)
+def test_generated_source_compiles_for_sm100a(name, tmp_path, monkeypatch):
+    monkeypatch.setenv("TGCB_CACHE_DIR", str(tmp_path))
+    build = {
+        "cone": lambda: workloads.cone_graph(ir.Builder),
+        "mlp": lambda: workloads.mlp_graph(ir.Builder, rows=1024),
+        "int8": lambda: workloads.int8_linear_graph(ir.Builder, ir.INT8, ir.INT32, ir.FLOAT32, rows=256),
+        "grad_small": lambda: load_graph("train_grad_small"),
+        "sum": lambda: workloads.sum_graph(ir.Builder, n=1 << 20),
+    }
+    g = build[name]() if name in build else load_graph(name)
+    cubin = runtime.compile_source(runtime.source_of(g))
+    assert cubin[:4] == b"\x7fELF"
+
+
+def test_refusals():
+    b = ir.Builder()
+    x = b.input(["n", 4], name="x")
+    g = b.finish(b.exp(x))
+    with pytest.raises(CodegenError):
+        runtime.generate(g)
+    b = ir.Builder()
+    x = b.input([4, 4], ir.FLOAT64, name="x")
+    g = b.finish(b.matmul(x, x))
+    with pytest.raises(CodegenError):
+        runtime.generate(g)
+    b = ir.Builder()
+    x = b.input([4, 4], ir.INT32, name="x")
+    g = b.finish(b.matmul(x, x))
+    with pytest.raises(CodegenError, match="int8"):
+        runtime.generate(g)
+
+
+def test_odd_gemm_rows_use_the_simt_fallback():
+    b = ir.Builder()
+    a = b.input([5, 3], name="a")
+    w = b.input([3, 7], name="w")
+    mod = runtime.generate(b.finish(b.matmul(a, w)))[3]
+    assert mod.steps[0].kind == "gemm" and "SIMT" in mod.steps[0].bracketing
+
+
+def test_compile_error_is_a_codegen_error():
+    with pytest.raises(CodegenError):
+        runtime.compile_source('extern "C" __global__ void k() { this is not cuda; }')

@@ -1,0 +1,123 @@
+"""The ahead-of-time kernels through the C-ABI: bit-exact float32 summation orders and the
+per-row int8 quantiser, against tgc's golden values and the oracle's restatements."""
+
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+from conftest import GOLDEN
+
+from oracle import bracketing
+from oracle import quantize as oq
+from tgcb import _lib, quantize, summation, workloads
+from tgcb.errors import ConfigError
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def summ():
+    with open(os.path.join(GOLDEN, "summation.json")) as f:
+        return json.load(f)
+
+
+def test_long_sum_bit_exact_to_tgc(cuda, summ):
+    """2^26 values with a 1e8 leader: pairwise and sequential equal tgc's own results."""
+    ls = summ["longsum"]
+    v, idx = workloads.longsum_input()
+    assert idx == ls["leader_index"]
+    vc = v.cuda()
+    p = summation.pairwise(vc)
+    s = summation.sequential(vc)
+    assert p == ls["pairwise"]
+    assert s == ls["sequential"]
+    exact = ls["exact"]
+    # the point of the bracketing: the tree is orders of magnitude closer to the exact sum
+    assert abs(p - exact) / exact < abs(s - exact) / exact
+
+
+def test_summation_vectors_bit_exact_to_tgc(cuda, summ):
+    gens = {
+        "uniform": lambda c, s: np.asarray(np.random.default_rng(s).uniform(0.5, 1.5, size=c), dtype=np.float32),
+        "mixed": lambda c, s: np.asarray([1e9, *np.random.default_rng(s).uniform(0.5, 1.5, size=c - 1)], dtype=np.float32),
+        "alternating": lambda c, s: np.asarray(np.random.default_rng(s).normal(0.0, 1.0, size=c), dtype=np.float32),
+    }
+    for vec in summ["vectors"]:
+        v = torch.from_numpy(gens[vec["kind"]](vec["count"], vec["seed"])).cuda()
+        assert summation.sequential(v) == vec["sequential"]
+        assert summation.pairwise(v) == vec["pairwise"]
+        assert summation.pairwise(v, block=3) == vec["pairwise_block_3"]
+
+
+@pytest.mark.parametrize("n", [1, 2, 7, 8, 9, 17, 255, 256, 257, 1000, 12345, 65537, 1000003, (1 << 21) + 3])
+@pytest.mark.parametrize("block", [1, 3, 8, 16])
+def test_pairwise_any_length_any_block(cuda, n, block):
+    v = torch.rand(n, generator=torch.Generator().manual_seed(n + block)) - 0.3
+    assert summation.pairwise(v.cuda(), block) == bracketing.pairwise(v.numpy(), block)
+
+
+@pytest.mark.parametrize("n", [1, 5, 1000, 65537])
+def test_sequential_any_length(cuda, n):
+    v = torch.rand(n, generator=torch.Generator().manual_seed(n))
+    assert summation.sequential(v.cuda()) == bracketing.sequential(v.numpy())
+
+
+def test_pairwise_on_an_unaligned_view(cuda):
+    v = torch.rand(4099, generator=torch.Generator().manual_seed(1))
+    vc = v.cuda()[3:]
+    assert summation.pairwise(vc) == bracketing.pairwise(v.numpy()[3:])
+
+
+def test_summation_input_checks(cuda):
+    with pytest.raises(ConfigError, match="nothing to sum"):
+        summation.pairwise(torch.empty(0, device="cuda"))
+    with pytest.raises(ConfigError, match="float32"):
+        summation.sequential(torch.ones(4, dtype=torch.float64, device="cuda"))
+    with pytest.raises(ConfigError, match="vector"):
+        summation.pairwise(torch.ones(2, 2, device="cuda"))
+
+
+def test_pairwise_rejects_short_scratch(cuda):
+    lib = _lib.load()
+    v = torch.ones(1 << 16, device="cuda")
+    out = torch.empty(1, device="cuda")
+    rc = lib.tgcb_sum_pairwise_f32(ctypes.c_void_p(v.data_ptr()), v.numel(), 8, ctypes.c_void_p(out.data_ptr()),
+                                   ctypes.c_void_p(out.data_ptr()), 4, None)
+    assert rc == _lib.TGCB_E_INVALID
+    assert "scratch" in _lib.last_error()
+
+
+def test_quantiser_bit_exact_to_tgc(cuda):
+    gold = np.load(os.path.join(GOLDEN, "quantize.npz"))
+    for name in ("randn", "weights_t", "edge"):
+        x = torch.from_numpy(gold[f"{name}/x"]).cuda()
+        q, s = quantize.quantise_rows(x)
+        assert np.array_equal(q.cpu().numpy().astype(np.float32), gold[f"{name}/q"])
+        assert np.array_equal(s.cpu().numpy(), gold[f"{name}/scale"].astype(np.float32))
+
+
+@pytest.mark.parametrize("rows,cols", [(3, 1), (17, 1000), (64, 4096), (5, 5000)])
+def test_quantiser_shapes(cuda, rows, cols):
+    x = torch.randn(rows, cols, generator=torch.Generator().manual_seed(cols)) * 3
+    q, s = quantize.quantise_rows(x.cuda())
+    qo, so = oq.quantise_rows(x.numpy())
+    assert np.array_equal(q.cpu().numpy(), qo)
+    assert np.array_equal(s.cpu().numpy(), so)
+
+
+def test_quantiser_input_checks(cuda):
+    with pytest.raises(ConfigError):
+        quantize.quantise_rows(torch.ones(4, device="cuda"))
+    with pytest.raises(ConfigError):
+        quantize.quantise_rows(torch.ones(0, 3, device="cuda"))
+
+
+def test_device_status_stays_clear(cuda):
+    st = ctypes.c_int(-1)
+    _lib.check(_lib.load().tgcb_status(1, ctypes.byref(st)), "tgcb_status")
+    assert st.value == 0
