@@ -138,6 +138,25 @@ int tgcb_sum_pairwise_f32(const float* x, uint64_t n, int block, float* out, voi
 /* Sequential sum from 0.0f left to right, bit-exact to tgc/analysis/summation.py:56-61. */
 int tgcb_sum_sequential_f32(const float* x, uint64_t n, float* out, void* stream);
 
+/* No counterpart in the reference: tgc runs on the CPU and never needs device memory.
+ *
+ * The pairwise sum above, for callers that cannot allocate device memory themselves: code
+ * running inside a host callback or a memory-pool-restricted service, or plugins whose
+ * allocator belongs to someone else. Takes the same x, n, block, out and stream as
+ * tgcb_sum_pairwise_f32 and gives the same result, but uses a scratch array built into the
+ * library (TGCB_NOALLOC_SCRATCH_BYTES per device, held by every GPU that loads the library
+ * until the process exits) instead of caller scratch, and calls no allocator.
+ *   - Limit: n must need at most TGCB_NOALLOC_SCRATCH_BYTES of scratch, see
+ *     tgcb_sum_pairwise_scratch_bytes(n, block); that is up to 2^28 values at block 8.
+ *     Larger n is refused with TGCB_E_INVALID before anything is launched.
+ *   - The first call on a device looks up the array's device address with that device
+ *     current; make that first call before any stream capture.
+ *   - Every call shares the one array, so calls whose kernels overlap on the GPU (different
+ *     streams, or different host threads) race; serialise them. Nothing in the array has to
+ *     start at zero: each level of the tree writes every partial it later reads. */
+#define TGCB_NOALLOC_SCRATCH_BYTES (1u << 20)
+int tgcb_sum_pairwise_f32_noalloc(const float* x, uint64_t n, int block, float* out, void* stream);
+
 /* Per-row symmetric int8 quantisation, bit-exact to quantize.symmetric_scheme + quantise
  * applied per row (tgc/analysis/quantize.py:90-128, 229-240): m = max|row| in float32,
  * scale = float((double)m / 127) (1.0f for an all-zero row), q = rint(x / scale) clamped to

@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 #include <string>
 
 #include "tgcb.h"
@@ -282,3 +283,47 @@ int tgcb_quantise_rows_i8(const float* x, int64_t rows, int64_t cols, int8_t* q,
 }
 
 }  // extern "C"
+
+// ----------------------------------------------------------------------------- no-alloc variant
+//
+// For callers that cannot allocate device memory (see include/tgcb.h): the pairwise sum's
+// partials live in this file-scope device array instead of caller scratch. On the host its
+// name is only a stand-in for the symbol, never a device address; the address is looked up
+// once per device with cudaGetSymbolAddress and then passed to the unchanged entry point.
+static __device__ __align__(256) unsigned char g_noalloc_pairwise_scratch[TGCB_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kNoAllocDevices = 16;
+void* g_noalloc_scratch_ptr[kNoAllocDevices] = {};
+std::mutex g_noalloc_mutex;
+}  // namespace
+
+extern "C" int tgcb_sum_pairwise_f32_noalloc(const float* x, uint64_t n, int block, float* out, void* stream) {
+  if (x == nullptr || out == nullptr)
+    return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_pairwise_f32_noalloc", "null pointer");
+  if (n == 0) return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_pairwise_f32_noalloc", "there is nothing to sum");
+  if (block < 1)
+    return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_pairwise_f32_noalloc", "a block must hold at least one value");
+  const size_t need = tgcb_sum_pairwise_scratch_bytes(n, block);
+  if (need > TGCB_NOALLOC_SCRATCH_BYTES)
+    return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_pairwise_f32_noalloc",
+                              "this length needs more scratch than the built-in 1 MiB array (at most 2^28 values at "
+                              "block 8); use tgcb_sum_pairwise_f32 with caller scratch");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return report(TGCB_E_CUDA, "cudaGetDevice", e);
+  if (dev < 0 || dev >= kNoAllocDevices)
+    return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_pairwise_f32_noalloc", "device index out of range");
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_scratch_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_pairwise_scratch);
+      if (e != cudaSuccess) return report(TGCB_E_CUDA, "cudaGetSymbolAddress", e);
+      g_noalloc_scratch_ptr[dev] = p;
+    }
+    scratch = g_noalloc_scratch_ptr[dev];
+  }
+  return tgcb_sum_pairwise_f32(x, n, block, out, scratch, TGCB_NOALLOC_SCRATCH_BYTES, stream);
+}
