@@ -1,7 +1,7 @@
 // Persistent tcgen05 GEMM for sm_100a: D[M,N] = A[M,K] @ B[K,N] with a generated epilogue.
 //
 // One CTA per SM loops over 128x256 output tiles. Warp 0 is the TMA producer, warp 1 issues
-// tcgen05.mma from one thread, warps 2..9 are the epilogue. Operands are staged through a
+// tcgen05.mma from one thread, warps 2..17 are the epilogue. Operands are staged through a
 // 4-deep ring of shared-memory stages, each 128 bytes of K per row (32 tf32 or 128 int8
 // values) in the 128-byte swizzled layout that TMA writes and the UMMA descriptors read.
 // The accumulator lives in tensor memory: two 256-column fp32/int32 buffers, so the
@@ -29,14 +29,13 @@ constexpr int STAGES = 4;
 constexpr int ROW_BYTES = 128;
 constexpr int A_STAGE = BM * ROW_BYTES;   // 16 KB
 constexpr int B_STAGE = BN * ROW_BYTES;   // 32 KB
-constexpr int EPI_WARPS = 8;
+constexpr int EPI_WARPS = 16;  // four per TMEM lane quadrant, 64 columns each
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int BAR_BYTES = 256;
-// Each epilogue warp transposes 32 rows x 16 columns through shared memory (row pitch 17
-// words: conflict-free writes of a row per lane and reads of a column per lane).
-constexpr int STAGE_PITCH = 17;
-constexpr int EPI_STAGE_BYTES = EPI_WARPS * 32 * STAGE_PITCH * 4;
+// Each epilogue warp transposes 32 rows x 8 columns at a time through shared memory.
+constexpr int STAGE_WORDS = 32 * 8;
+constexpr int EPI_STAGE_BYTES = EPI_WARPS * STAGE_WORDS * 4;
 constexpr int SMEM_BYTES = STAGES * (A_STAGE + B_STAGE) + BAR_BYTES + EPI_STAGE_BYTES + 1024;
 constexpr unsigned long long WAIT_BUDGET_NS = 4000000000ull;  // 4 s
 
@@ -135,6 +134,13 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -215,8 +221,8 @@ __device__ __forceinline__ void gemm_body(const TgcbArgs& args, const TgcbTmaDes
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = blockIdx.x; tile < NUM_TILES; tile += gridDim.x) {
-        const int tm = tile % TILES_M;
-        const int tn = tile / TILES_M;
+        const int tm = tile / TILES_N;  // N fastest: CTAs running together share A panels in L2
+        const int tn = tile % TILES_N;
         for (int kb = 0; kb < NUM_KB; ++kb) {
           if (!bar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.status, TGCB_STATUS_TIMEOUT_PRODUCER)) goto producer_done;
           bar_arrive_expect(full_bar(stage), STAGE_TX);
@@ -288,14 +294,14 @@ __device__ __forceinline__ void gemm_body(const TgcbArgs& args, const TgcbTmaDes
     }
   } else {
     const int ew = warp - 2;
-    const int quad = warp & 3;
-    const int half = ew >> 2;  // which half of the 256 columns this warp drains
-    uint32_t* stage = reinterpret_cast<uint32_t*>(smem + STAGES * (A_STAGE + B_STAGE) + BAR_BYTES) + ew * 32 * STAGE_PITCH;
+    const int quad = warp & 3;         // TMEM lanes 32*quad .. 32*quad+31 (the warp's rows)
+    const int part = ew >> 2;          // which quarter of the 256 columns this warp drains
+    uint32_t* stage = reinterpret_cast<uint32_t*>(smem + STAGES * (A_STAGE + B_STAGE) + BAR_BYTES) + ew * STAGE_WORDS;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < NUM_TILES; tile += gridDim.x) {
-      const int tm = tile % TILES_M;
-      const int tn = tile / TILES_M;
+      const int tm = tile / TILES_N;
+      const int tn = tile % TILES_N;
       bool ok = true;
       if (lane == 0) ok = bar_wait(tfull_bar(acc), acc_phase, abort_flag, args.status, TGCB_STATUS_TIMEOUT_EPILOGUE);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -303,20 +309,21 @@ __device__ __forceinline__ void gemm_body(const TgcbArgs& args, const TgcbTmaDes
       tc_fence_after();
       const long long row0 = (long long)tm * BM + quad * 32;
 #pragma unroll 1
-      for (int chunk = half * (BN / 32); chunk < (half + 1) * (BN / 32); ++chunk) {
-        uint32_t r[16];
-        tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + chunk * 16), r);
-        // lane = row on the way in; lanes run along columns on the way out, so the
-        // epilogue's side-input loads and its stores are coalesced along the row.
+      for (int chunk = part * (BN / 32); chunk < (part + 1) * (BN / 32); ++chunk) {
+        uint32_t r[8];
+        tmem_ld8(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + chunk * 8), r);
+        // lane = row on the way in; on the way out each lane takes one column of one of four
+        // rows, so side-input loads and stores run along rows (32-byte segments). The 8-word
+        // rows are XOR-swizzled by row/4 so both the writes and the reads are conflict-free.
 #pragma unroll
-        for (int j = 0; j < 16; ++j) stage[lane * STAGE_PITCH + j] = r[j];
+        for (int j = 0; j < 8; ++j) stage[lane * 8 + (j ^ (lane >> 2))] = r[j];
         __syncwarp();
-        const long long col0 = (long long)tn * BN + chunk * 16;
-#pragma unroll 4
-        for (int it = 0; it < 16; ++it) {
-          const int rr = 2 * it + (lane >> 4);
-          const int cc = lane & 15;
-          const uint32_t bits = stage[rr * STAGE_PITCH + cc];
+        const long long col0 = (long long)tn * BN + chunk * 8;
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int rr = 4 * it + (lane >> 3);
+          const int cc = lane & 7;
+          const uint32_t bits = stage[rr * 8 + (cc ^ it)];
           if constexpr (INT8) {
             Epi::apply(args, row0 + rr, col0 + cc, (int)bits);
           } else {

@@ -42,6 +42,7 @@ from tgcb.errors import CodegenError
 from tgcb.expr import ExprBuilder, _broadcast_index, ctype, delinearise
 
 NUM_SMS = 148
+GEMM_THREADS = 576  # tgcb_gemm::THREADS: TMA warp, MMA warp, 16 epilogue warps
 
 # Placeholder for the base pointer of a materialised value; replaced once the plan exists.
 def PTR(name: str) -> str:
@@ -853,13 +854,13 @@ class Lowering:
         tma_ok = all((op.cols * op.elem_bytes) % 16 == 0 for op in (opa, opb))
         if tma_ok:
             kernel = (
-                f'extern "C" __global__ void __launch_bounds__(320, 1) {kname}(const TgcbArgs args, '
+                f'extern "C" __global__ void __launch_bounds__({GEMM_THREADS}, 1) {kname}(const TgcbArgs args, '
                 "const __grid_constant__ TgcbTmaDesc ta, const __grid_constant__ TgcbTmaDesc tb) {\n"
                 f"  tgcb_gemm::gemm_body<{M}, {N}, {K}, {'true' if is_int else 'false'}, "
                 f"{'true' if opa.mn_major else 'false'}, {'true' if opb.mn_major else 'false'}, {epi_name}>(args, &ta, &tb);\n}}\n"
             )
             tiles = ((M + 127) // 128) * ((N + 255) // 256)
-            launch = Launch(kname, (max(1, min(tiles, NUM_SMS)), 1, 1), (320, 1, 1), smem=-1, gemm=(opa, opb))
+            launch = Launch(kname, (max(1, min(tiles, NUM_SMS)), 1, 1), (GEMM_THREADS, 1, 1), smem=-1, gemm=(opa, opb))
             how = "tcgen05." + ("kind::i8, int32 accumulator in TMEM (exact)" if is_int else "kind::tf32, fp32 accumulator in TMEM, K in steps of 8")
         else:
             kernel = self._gemm_simt_kernel(kname, epi_name, M, N, K, is_int, a_base, a_flip, b_base, b_flip)

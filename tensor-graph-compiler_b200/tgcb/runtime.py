@@ -42,8 +42,8 @@ SUPPORTED_OPS = {
     "transpose", "broadcast_to", "concat", "slice", "constant", "print", "assert_finite",
 }
 # tgcb_gemm::SMEM_BYTES: 4 stages of (128 + 256) rows x 128 B, barriers, the epilogue
-# transpose tiles (8 warps x 32 x 17 words) and 1 KB of alignment slack.
-GEMM_SMEM = 4 * (128 + 256) * 128 + 256 + 8 * 32 * 17 * 4 + 1024
+# transpose tiles (16 warps x 32 x 8 words) and 1 KB of alignment slack.
+GEMM_SMEM = 4 * (128 + 256) * 128 + 256 + 16 * 32 * 8 * 4 + 1024
 _PLACEHOLDER = re.compile(r"@P<([^>]+)>@")
 
 TORCH_DTYPES = {}
