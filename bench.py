@@ -10,9 +10,10 @@ step is one execution of the compiled graph. Other workloads: ``cone`` (x [4096,
 exp -> three row reductions), ``int8`` (per-token/per-channel int8 linear
 8192x4096x4096), ``longsum`` (bit-exact pairwise sum of 2^26 floats).
 
-Multi-GPU (torchrun, one process per GPU, NCCL): every rank runs its own shard of rows, so
-work per GPU is fixed ("weak"); ``value`` = executions by all ranks / the slowest rank's
-device time. Timing: W warm-up steps; then K steps, each timed with CUDA events recorded on
+Multi-GPU (torchrun, one process per GPU, NCCL): for the forward workloads every rank runs
+its own shard of rows, so work per GPU is fixed ("weak") and ``value`` = executions by all
+ranks / the slowest rank's device time; ``train`` splits one 65536-row global batch over the
+ranks ("strong") and averages the gradients with NCCL, one unit being one global step. Timing: W warm-up steps; then K steps, each timed with CUDA events recorded on
 the stream the kernels run on (one event around every kernel, tgcb_plan_run_profiled); L2
 flushed before every timed step outside the events (a 256 MiB write, then a 256 MiB read so
 the flush leaves no dirty lines to be written back inside a timed kernel); a bounded delay
@@ -57,7 +58,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["tgcb", "reference"], default="tgcb")
-    p.add_argument("--workload", choices=["mlp", "cone", "int8", "longsum"], default="mlp")
+    p.add_argument("--workload", choices=["mlp", "cone", "int8", "longsum", "train"], default="mlp")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
@@ -392,7 +393,103 @@ class LongSumWorkload:
         return {}
 
 
-WORKLOADS = {"mlp": MlpWorkload, "cone": ConeWorkload, "int8": Int8Workload, "longsum": LongSumWorkload}
+class TrainWorkload:
+    """Reverse-mode step of the MLP block: MSE over a 65536-row global batch, sharded over ranks.
+
+    Each rank runs tgc's gradient graph of its shard (tgcb.grad + compile_graph) and the four
+    gradients are averaged with NCCL, each all-reduce starting when its gradient is final.
+    Total work is fixed as N grows ("strong"); one unit is one global step.
+    """
+
+    name = "train"
+    unit = "train steps/s"
+    dtype = "tf32"
+    scaling = "strong"
+    global_rows = 65536
+    payload = 2 * 1024 * 4096 * 4 + 4096 * 4 + 1024 * 4
+
+    def __init__(self, rank: int):
+        self.rank = rank
+
+    def config(self):
+        return {
+            "workload": "MLP block training step: d/dW of mean((mlp(x)-target)^2), x,target [65536,1024] batch-sharded, "
+            "W1 [1024,4096], W2 [4096,1024]; gradients averaged by NCCL all-reduce",
+            "global_rows": self.global_rows,
+            "flops_per_step": 5 * 2 * self.global_rows * 1024 * 4096,
+            "allreduce_bytes": self.payload,
+            "l2": L2_NOTE,
+        }
+
+    def units_per_step(self, n: int) -> int:
+        return 1
+
+    def setup(self, device, dist=None, world: int = 1):
+        import torch
+
+        from tgcb import parallel, workloads
+
+        self.world = world
+        self.step_obj = parallel.DataParallelTrainStep(self.global_rows, world, self.rank, dist=dist, device=device)
+        self.g = self.step_obj.graph
+        feeds = workloads.mlp_inputs(rows=self.global_rows, target=True)
+        x, t = self.step_obj.shard(feeds["x"], feeds["target"])
+        self.cpu_feeds = {**{k: feeds[k] for k in parallel.GRADS}, "x": x.contiguous(), "target": t.contiguous()}
+        self.dev_feeds = {k: v.to(device) for k, v in self.cpu_feeds.items()}
+        self.host_feeds = {k: v.pin_memory() for k, v in self.cpu_feeds.items()}
+        outs = self.step_obj.step(self.dev_feeds)
+        self.out_host = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+        torch.cuda.synchronize()
+        self.compiled = self.step_obj.compiled
+
+    def launches_per_step(self) -> int:
+        return self.compiled.launches_per_call
+
+    def step_profiled(self) -> list[float]:
+        import torch
+
+        main = torch.cuda.current_stream()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        timing = []
+        s.record(main)
+        self.step_obj.step(self.dev_feeds, timing=timing)
+        e.record(main)
+        e.synchronize()
+        per = [a.elapsed_time(b) for a, b in timing]
+        total = s.elapsed_time(e)
+        return per + [max(0.0, total - sum(per))]
+
+    def step_e2e(self) -> None:
+        outs = self.step_obj.step(self.host_feeds)
+        for o, h in zip(outs, self.out_host, strict=True):
+            h.copy_(o, non_blocking=True)
+
+    def h2d_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self.host_feeds.values())
+
+    def d2h_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self.out_host)
+
+    def kernel_work(self) -> list[dict]:
+        return GraphWorkload.kernel_work(self) + [
+            {"name": "exposed NCCL all-reduce and gaps", "kind": "allreduce", "bound": "nvlink", "work": self.payload}
+        ]
+
+    def cpu_program(self):
+        """One 8192-row shard of the step by the oracle (the full 65536 rows take minutes on a CPU)."""
+        from oracle import interp
+        from tgcb import parallel, workloads
+
+        g = parallel.train_graph(8192)
+        feeds = workloads.mlp_inputs(rows=8192, target=True)
+        prog = interp.generated_python_program(g)
+        scale = self.global_rows // 8192
+        self.cpu_scale = scale
+        return lambda _feeds: prog(feeds)
+
+
+WORKLOADS = {"mlp": MlpWorkload, "cone": ConeWorkload, "int8": Int8Workload, "longsum": LongSumWorkload,
+             "train": TrainWorkload}
 
 
 # ----------------------------------------------------------------------------- cpu baseline
@@ -414,7 +511,7 @@ def cpu_baseline(wl, budget_s: float) -> dict:
         times.append(time.perf_counter() - t0)
         if time.perf_counter() - start > budget_s or len(times) >= 50:
             break
-    med = statistics.median(times)
+    med = statistics.median(times) * getattr(wl, "cpu_scale", 1)
     what = (
         "oracle/bracketing.c's restatement of tgc's summation.pairwise (1 thread)"
         if wl.name == "longsum"
@@ -425,7 +522,8 @@ def cpu_baseline(wl, budget_s: float) -> dict:
         "unit": wl.unit,
         "cores": 1 if wl.name == "longsum" else torch.get_num_threads(),
         "kind": "port",
-        "sample": f"{len(times)} full executions of the same workload by {what}; median {med:.4f} s",
+        "sample": f"{len(times)} executions by {what}; median {med:.4f} s per unit"
+        + (f" (one 8192-row shard timed, x{wl.cpu_scale} for the 65536-row step)" if getattr(wl, "cpu_scale", 1) > 1 else ""),
     }
 
 
@@ -471,7 +569,12 @@ def main() -> int:
         dist = dist_mod
 
     wl = WORKLOADS[args.workload](rank)
-    wl.setup(device)
+    if args.workload == "train":
+        wl.setup(device, dist, n)
+    else:
+        wl.setup(device)
+    scaling = getattr(wl, "scaling", "weak")
+    units = wl.units_per_step(n) if hasattr(wl, "units_per_step") else n
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     flush_read = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
     flush_sink = torch.empty((), dtype=torch.float32, device=device)
@@ -539,7 +642,7 @@ def main() -> int:
         pk, src = peaks()
         work = wl.kernel_work()
         shares = [p / sum(per_launch) for p in per_launch]
-        dom = max(range(len(per_launch)), key=lambda i: per_launch[i])
+        dom = max((i for i in range(len(per_launch)) if work[i]["bound"] != "nvlink"), key=lambda i: per_launch[i])
         dk = work[dom]
         avg_ms = per_launch[dom] / args.steps
         if dk["bound"] == "tensor":
@@ -556,7 +659,7 @@ def main() -> int:
             achieved = dk["work"] / (avg_ms * 1e-3) / 1e9
             unit = "GB/s"
             peak_note = f"{src} STREAM-style copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"
-        value = n * args.steps / (total_ms * 1e-3)
+        value = units * args.steps / (total_ms * 1e-3)
         hbm_bytes = sum(w["work"] for w in work if w["bound"] == "hbm")
         hbm_ms = sum(per_launch[i] for i, w in enumerate(work) if w["bound"] == "hbm") / args.steps
         result = {
@@ -568,11 +671,13 @@ def main() -> int:
             "warmup": warm,
             "ms_per_step": round(total_ms / args.steps, 4),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": scaling,
             "vs_baseline": None,
             "dtype": wl.dtype,
             "data": "synthetic: seeded torch.randn inputs and random-init weights of the workload's shapes",
-            "config": {**wl.config(), "parallelism": f"dp{n}: independent row shards per GPU, no collective"},
+            "config": {**wl.config(), "parallelism": f"dp{n}: " + (
+                f"{wl.global_rows // n} rows per GPU, gradients averaged by NCCL all-reduce overlapped with the backward"
+                if args.workload == "train" else "independent row shards per GPU, no collective")},
             "roofline": {
                 "bound": dk["bound"],
                 "kernel": dk["name"],
@@ -593,7 +698,7 @@ def main() -> int:
                 for i, w in enumerate(work)
             ],
             "e2e": {
-                "value": round(n * args.steps / (e2e_ms * 1e-3), 3),
+                "value": round(units * args.steps / (e2e_ms * 1e-3), 3),
                 "unit": wl.unit,
                 "h2d_bytes_per_step": wl.h2d_bytes(),
                 "d2h_bytes_per_step": wl.d2h_bytes(),
@@ -620,6 +725,8 @@ def run_reference(args, n: int) -> int:
         from tgcb import workloads
 
         wl.v, _ = workloads.longsum_input(wl.n)
+    elif args.workload == "train":
+        wl.cpu_feeds = {}
     else:
         wl.g = wl.graph()
         wl.cpu_feeds = wl.feeds()
@@ -633,7 +740,7 @@ def run_reference(args, n: int) -> int:
         t0 = time.perf_counter()
         prog(feeds)
         times.append(time.perf_counter() - t0)
-    total = sum(times)
+    total = sum(times) * getattr(wl, "cpu_scale", 1)
     value = args.steps / total
     cores = 1 if args.workload == "longsum" else torch.get_num_threads()
     line = {
@@ -646,7 +753,7 @@ def run_reference(args, n: int) -> int:
         "warmup": warm,
         "ms_per_step": round(total / args.steps * 1e3, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": getattr(wl, "scaling", "weak"),
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic: seeded torch.randn inputs and random-init weights of the workload's shapes",

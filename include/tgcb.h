@@ -112,6 +112,14 @@ int tgcb_plan_run(tgcb_plan* p, void* arena, const void* const* inputs, int n_in
 /* Number of launches a plan queues per run. */
 int tgcb_plan_launch_count(const tgcb_plan* p);
 
+/* tgcb_plan_run restricted to launches [first, first + count). Running the ranges of a plan
+ * back to back on one stream is the same as tgcb_plan_run; a data-parallel step splits its
+ * plan where a gradient becomes final and starts that gradient's all-reduce on another
+ * stream while the remaining launches run (tgc/parallel/collective.py:339-379 models this
+ * overlap; here it is executed). */
+int tgcb_plan_run_range(tgcb_plan* p, int first, int count, void* arena, const void* const* inputs, int n_inputs,
+                        void* stream);
+
 /* tgcb_plan_run with a CUDA event recorded on `stream` before the first launch and after
  * every launch; waits for the stream and writes each launch's device time in milliseconds to
  * ms[0 .. launch_count). The measurement tgc's runtime/profile.py:91-145 takes with

@@ -338,6 +338,23 @@ int tgcb_plan_run(tgcb_plan* p, void* arena, const void* const* inputs, int n_in
   return TGCB_OK;
 }
 
+int tgcb_plan_run_range(tgcb_plan* p, int first, int count, void* arena, const void* const* inputs, int n_inputs,
+                        void* stream) {
+  DeviceState* st = nullptr;
+  TgcbArgs args;
+  int rc = prepare_run(p, arena, inputs, n_inputs, &st, &args);
+  if (rc != TGCB_OK) return rc;
+  if (first < 0 || count < 0 || (size_t)first + (size_t)count > p->launches.size())
+    return fail(TGCB_E_INVALID, "launch range [%d, %d) is outside a plan of %zu launches", first, first + count,
+                p->launches.size());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int i = first; i < first + count; ++i) {
+    rc = launch_one(st, p->launches[i], args, arena, inputs, n_inputs, s);
+    if (rc != TGCB_OK) return rc;
+  }
+  return TGCB_OK;
+}
+
 int tgcb_plan_run_profiled(tgcb_plan* p, void* arena, const void* const* inputs, int n_inputs, void* stream,
                            float* ms) {
   if (ms == nullptr) return fail(TGCB_E_INVALID, "tgcb_plan_run_profiled: null output");

@@ -88,6 +88,10 @@ SIGNATURES = {
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_float)],
     ),
     "tgcb_delay": (ctypes.c_int, [ctypes.c_uint64, ctypes.c_void_p]),
+    "tgcb_plan_run_range": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_void_p],
+    ),
     "tgcb_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "tgcb_sum_pairwise_scratch_bytes": (ctypes.c_size_t, [ctypes.c_uint64, ctypes.c_int]),
     "tgcb_sum_pairwise_f32": (

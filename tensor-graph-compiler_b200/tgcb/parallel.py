@@ -1,0 +1,146 @@
+"""Batch sharding across the GPUs of one box, with the gradient all-reduce done for real.
+
+tgc simulates data parallelism in one process: ``row_parallel`` splits the batch rows over
+devices with the weights replicated (tgc/parallel/shard.py:39-123), ``shard`` cuts tensors with
+``torch.chunk`` and refuses a split that is not even (shard.py:57-67), and
+tgc/parallel/collective.py prices the gradient all-reduce with a ring model and its overlap
+with the backward pass (collective.py:76-113, 339-379). Here each rank is one process driving
+one GPU; it compiles the gradient graph of its own shard (``tgcb.grad.gradient`` of the MLP's
+mean-squared error over shard_rows rows, lowered by ``tgcb.runtime``), runs it, and averages
+the four gradients over ranks with NCCL over NVLink (``torch.distributed``; AVG, since every
+shard's loss is a mean over the same number of rows, so the global gradient is the mean of the
+shard gradients). Each gradient's all-reduce is started on a separate stream as soon as the
+launch that finalises it has been queued, so it overlaps the launches that remain.
+
+The same code runs with the ``gloo`` backend on CPU ranks when ``executor`` replaces the GPU
+plan (tests use the oracle there), which is how the host-side sharding and averaging logic is
+tested without GPUs.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+
+from tgcb import grad, ir, workloads
+from tgcb.errors import ConfigError, PassError
+
+GRADS = ("w1", "b1", "w2", "b2")
+
+
+def shard_rows(total_rows: int, devices: int, rank: int) -> tuple[int, int]:
+    """(first row, row count) of ``rank``'s contiguous block; refuses an uneven split like tgc."""
+    if devices < 1:
+        raise ConfigError(f"there has to be at least one device, got {devices}")
+    if not 0 <= rank < devices:
+        raise ConfigError(f"rank {rank} is outside {devices} devices")
+    if total_rows % devices:
+        raise PassError(f"{total_rows} does not divide evenly over {devices} devices")
+    n = total_rows // devices
+    return rank * n, n
+
+
+def ring_time(size_bytes: int, devices: int, bytes_per_second: float, latency_seconds: float) -> float:
+    """tgc's ring all-reduce model (collective.py:76-88) with a given link: 2(n-1) steps of size/n."""
+    if devices <= 1:
+        return 0.0
+    return 2 * (devices - 1) * (latency_seconds + (size_bytes / devices) / bytes_per_second)
+
+
+def ring_volume(size_bytes: int, devices: int) -> float:
+    """Bytes each device sends in a ring all-reduce (collective.py:113-122)."""
+    return 0.0 if devices <= 1 else 2.0 * size_bytes * (devices - 1) / devices
+
+
+def train_graph(rows: int, d: int = 1024, f: int = 4096):
+    """The gradient graph of mean((mlp(x) - target)^2) over ``rows`` rows w.r.t. w1, b1, w2, b2."""
+    return grad.gradient(workloads.mlp_graph(ir.Builder, rows=rows, d=d, f=f, loss=True), list(GRADS), seed_is_input=False).graph
+
+
+class DataParallelTrainStep:
+    """One data-parallel gradient step of the MLP block (the reverse-mode workload).
+
+    ``global_rows`` are split into ``world`` contiguous shards; rank ``rank`` owns rows
+    [first, first + shard) of x and target. ``step(feeds)`` takes this rank's shard of x and
+    target plus the replicated weights and returns the globally averaged gradients
+    (dW1, db1, dW2, db2), identical on every rank.
+    """
+
+    def __init__(self, global_rows: int, world: int, rank: int, *, d: int = 1024, f: int = 4096, dist=None,
+                 device=None, executor: Callable | None = None):
+        self.global_rows = global_rows
+        self.world = world
+        self.rank = rank
+        self.first, self.rows = shard_rows(global_rows, world, rank)
+        self.dist = dist
+        self.graph = train_graph(self.rows, d, f)
+        self.executor = executor
+        if executor is None:
+            import torch
+
+            from tgcb.runtime import compile_graph
+
+            self.torch = torch
+            self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+            self.compiled = compile_graph(self.graph, device=self.device.index)
+            self.arena = self.compiled.new_arena()
+            self.comm = torch.cuda.Stream(device=self.device)
+            # where each gradient becomes final: split the plan there
+            writers = self.compiled.launch_writers()
+            outs = list(self.compiled.module.output_names)
+            self.finals = sorted({writers[o] for o in outs})
+            self.out_at = {k: [i for i, o in enumerate(outs) if writers[o] == k] for k in self.finals}
+
+    def shard(self, x, target):
+        """This rank's rows of the global batch."""
+        return x[self.first : self.first + self.rows], target[self.first : self.first + self.rows]
+
+    def _average(self, tensors: list) -> None:
+        if self.dist is None or self.world == 1:
+            return
+        if self.dist.get_backend() == "nccl":
+            for t in tensors:
+                self.dist.all_reduce(t, op=self.dist.ReduceOp.AVG)
+        else:
+            for t in tensors:
+                self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+                t.div_(self.world)
+
+    def step(self, feeds: dict, timing: list | None = None) -> list:
+        """Run the step. With ``timing`` (a list), one CUDA event pair per launch is appended to
+        it, recorded on the stream the launches run on."""
+        if self.executor is not None:
+            grads = [g.clone() for g in self.executor(self.graph, feeds)]
+            self._average(grads)
+            return grads
+        torch = self.torch
+        main = torch.cuda.current_stream(self.device)
+        ptrs = self.compiled.input_pointers(self.arena, feeds)
+        outs = self.compiled._outputs(self.arena, feeds)
+        done = 0
+        total = self.compiled.launches_per_call
+
+        def run(first: int, count: int) -> None:
+            if timing is None:
+                self.compiled.run_range(self.arena, ptrs, first, count, main)
+                return
+            for i in range(first, first + count):
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(main)
+                self.compiled.run_range(self.arena, ptrs, i, 1, main)
+                e.record(main)
+                timing.append((s, e))
+
+        for k in self.finals:
+            run(done, k + 1 - done)
+            done = k + 1
+            if self.dist is not None and self.world > 1:
+                ev = torch.cuda.Event()
+                ev.record(main)
+                with torch.cuda.stream(self.comm):
+                    self.comm.wait_event(ev)
+                    self._average([outs[i] for i in self.out_at[k]])
+        if done < total:
+            run(done, total - done)
+        if self.dist is not None and self.world > 1:
+            main.wait_stream(self.comm)
+        return outs

@@ -358,6 +358,24 @@ class CompiledGraph:
             _lib.check(rc, "running the compiled graph")
             return self._outputs(arena, feeds)
 
+    def run_range(self, arena, ptrs: list[int], first: int, count: int, stream) -> None:
+        """Queue launches [first, first+count) on ``stream`` with input addresses from ``input_pointers``."""
+        arr = (ctypes.c_void_p * max(1, len(ptrs)))(*ptrs)
+        rc = _lib.load().tgcb_plan_run_range(
+            self._plan, first, count, ctypes.c_void_p(arena.data_ptr()), arr, len(ptrs), ctypes.c_void_p(stream.cuda_stream)
+        )
+        _lib.check(rc, "running part of the compiled graph")
+
+    def launch_writers(self) -> dict[str, int]:
+        """For every materialised value, the index of the last launch of the step that writes it."""
+        out: dict[str, int] = {}
+        k = 0
+        for s in self.module.steps:
+            k += len(s.launches)
+            for w in s.writes:
+                out[w] = k - 1
+        return out
+
     def run_profiled(self, arena, feeds: dict, stream=None) -> tuple[list, list[float]]:
         """Run once with a CUDA event around every launch; returns (outputs, ms per launch).
 

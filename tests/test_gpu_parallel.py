@@ -1,0 +1,76 @@
+"""The reverse-mode training step on the GPU: one rank against the whole-batch oracle, and
+(when two GPUs are visible) two NCCL ranks against one. TF32 GEMMs: tolerance 5e-3 of the
+largest gradient entry."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import interp
+from tgcb import parallel, workloads
+
+pytestmark = pytest.mark.gpu
+TF32_TOL = 5e-3
+
+
+def rel_err(a, b) -> float:
+    a, b = a.detach().cpu().double(), b.detach().cpu().double()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+def test_single_rank_step_matches_oracle(cuda):
+    rows = 512
+    feeds = workloads.mlp_inputs(rows=rows, target=True)
+    step = parallel.DataParallelTrainStep(rows, 1, 0)
+    grads = step.step({k: v.cuda() for k, v in feeds.items()})
+    torch.cuda.synchronize()
+    step.compiled.check_status()
+    ref = interp.run(step.graph, feeds)
+    for g, r in zip(grads, ref, strict=True):
+        assert rel_err(g, r) < TF32_TOL
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_rank(rank: int, world: int, port: int, rows: int, out_dir: str) -> None:
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "NCCL_NVLS_ENABLE": "0"})
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=datetime.timedelta(seconds=60))
+    try:
+        feeds = workloads.mlp_inputs(rows=rows, target=True)
+        step = parallel.DataParallelTrainStep(rows, world, rank, dist=dist, device=dev)
+        x, t = step.shard(feeds["x"], feeds["target"])
+        shard = {**{k: feeds[k] for k in parallel.GRADS}, "x": x.contiguous(), "target": t.contiguous()}
+        grads = step.step({k: v.to(dev) for k, v in shard.items()})
+        torch.cuda.synchronize()
+        torch.save([g.cpu() for g in grads], os.path.join(out_dir, f"rank{rank}.pt"))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_nccl_ranks_match_the_whole_batch(tmp_path):
+    rows, world = 1024, 2
+    mp.start_processes(_nccl_rank, args=(world, _free_port(), rows, str(tmp_path)), nprocs=world, start_method="spawn")
+    feeds = workloads.mlp_inputs(rows=rows, target=True)
+    ref = interp.run(parallel.train_graph(rows), feeds)
+    r0 = torch.load(os.path.join(tmp_path, "rank0.pt"))
+    r1 = torch.load(os.path.join(tmp_path, "rank1.pt"))
+    for a, b, r in zip(r0, r1, ref, strict=True):
+        assert torch.equal(a, b)
+        assert rel_err(a, r) < TF32_TOL
