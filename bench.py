@@ -544,6 +544,19 @@ def read_traffic(workload: str, kernel_kind: str):
 
 
 def main() -> int:
+    # The JSON line must be the only thing on stdout; libraries (NCCL prints its version on
+    # rank 0) write to file descriptor 1, so point it at stderr and keep a private copy.
+    sys.stdout.flush()
+    json_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    sys.stdout = sys.stderr
+    try:
+        return _main(json_out)
+    finally:
+        json_out.flush()
+
+
+def _main(json_out) -> int:
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -553,7 +566,7 @@ def main() -> int:
     if args.impl == "reference":
         if rank != 0:
             return 0
-        return run_reference(args, n)
+        return run_reference(args, n, json_out)
 
     import torch
 
@@ -712,11 +725,11 @@ def main() -> int:
         dist.barrier()
         dist.destroy_process_group()
     if result is not None:
-        print(json.dumps(result), flush=True)
+        print(json.dumps(result), file=json_out, flush=True)
     return 0
 
 
-def run_reference(args, n: int) -> int:
+def run_reference(args, n: int, json_out) -> int:
     import torch
 
     torch.set_num_threads(os.cpu_count() or 1)
@@ -768,7 +781,7 @@ def run_reference(args, n: int) -> int:
         },
         "e2e": {"value": round(value, 4), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    print(json.dumps(line), file=json_out, flush=True)
     return 0
 
 
