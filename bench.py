@@ -61,6 +61,7 @@ def parse_args():
     p.add_argument("--workload", choices=["mlp", "cone", "int8", "longsum", "train"], default="mlp")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--train-rows", type=int, default=65536, help="global batch of the train workload (profiling uses a small one)")
     return p.parse_args()
 
 
@@ -530,15 +531,15 @@ def cpu_baseline(wl, budget_s: float) -> dict:
 # ----------------------------------------------------------------------------- main
 
 
-def read_traffic(workload: str, kernel_kind: str):
-    """DRAM bytes per launch of the dominant kernel, from the committed ncu summary."""
+def read_traffic(workload: str, kernel: str):
+    """DRAM bytes per launch of the dominant kernel, from the committed ncu summary (by kernel name)."""
     path = os.path.join(REPO, "profiles", "ncu_traffic.txt")
     if not os.path.exists(path):
         return None
     with open(path) as f:
         for line in f:
             parts = line.split()
-            if len(parts) >= 3 and not line.startswith("#") and parts[0] == workload and parts[1] == kernel_kind:
+            if len(parts) >= 3 and not line.startswith("#") and parts[0] == workload and parts[1] == kernel:
                 return int(parts[2])
     return None
 
@@ -583,6 +584,7 @@ def _main(json_out) -> int:
 
     wl = WORKLOADS[args.workload](rank)
     if args.workload == "train":
+        wl.global_rows = args.train_rows
         wl.setup(device, dist, n)
     else:
         wl.setup(device)
@@ -698,7 +700,7 @@ def _main(json_out) -> int:
                 "peak": round(peak, 1),
                 "unit": unit,
                 "frac": round(achieved / peak, 4),
-                "traffic": read_traffic(args.workload, dk["kind"]),
+                "traffic": read_traffic(args.workload, dk["name"]),
                 "peak_source": peak_note,
             },
             "hbm_kernels": {

@@ -658,23 +658,31 @@ class Lowering:
         t = ctype(node.output.dtype)
         opn = node.op.name
         cblocks = (C + 255) // 256
-        P = max(1, min((R + 15) // 16, (NUM_SMS * 4 + cblocks - 1) // cblocks))
+        # enough row blocks for ~8 CTAs per SM; each thread keeps UNROLL loads in flight
+        P = max(1, min((R + 15) // 16, (NUM_SMS * 8 + cblocks - 1) // cblocks))
         L = (R + P - 1) // P
         P = (R + L - 1) // L
         scratch = f"{name}__partials"
         self.scratch[scratch] = P * C * 8
         k1, k2 = self._kname("colpart"), self._kname("colfinal")
+        UNROLL = 8
         eb = ExprBuilder(self.values, self.producers, self._pointer_of, indent="    ")
-        v = eb.value(src, ("r", "c"))
-        body = "\n".join(eb.lines)
+        vals = [eb.value(src, (f"(r + {u})", "c")) for u in range(UNROLL)]
+        # loads of UNROLL rows are independent; the additions stay in row order
+        body = "\n".join(eb.lines + ["    " + self._acc_update(opn, "acc", v, t) for v in vals])
+        eb1 = ExprBuilder(self.values, self.producers, self._pointer_of, indent="    ")
+        v1 = eb1.value(src, ("r", "c"))
+        body1 = "\n".join(eb1.lines)
         s1 = (
             f'extern "C" __global__ void __launch_bounds__(256) {k1}(const TgcbArgs args) {{\n'
             f"  const long long c = (long long)blockIdx.x * 256 + threadIdx.x;\n"
             f"  if (c >= {C}LL) return;\n"
             f"  const long long r0 = (long long)blockIdx.y * {L}LL;\n"
-            f"  const long long r1 = min(r0 + {L}LL, {R}LL);\n"
+            f"  const long long r1 = tgcb_min_ll(r0 + {L}LL, {R}LL);\n"
             f"  {t} acc = {self._init(opn, t)};\n"
-            f"  for (long long r = r0; r < r1; ++r) {{\n{body}\n    {self._acc_update(opn, 'acc', v, t)}\n  }}\n"
+            f"  long long r = r0;\n"
+            f"  for (; r + {UNROLL} <= r1; r += {UNROLL}) {{\n{body}\n  }}\n"
+            f"  for (; r < r1; ++r) {{\n{body1}\n    {self._acc_update(opn, 'acc', v1, t)}\n  }}\n"
             f"  reinterpret_cast<{t}*>({PTR(scratch)})[blockIdx.y * {C}LL + c] = acc;\n}}\n"
         )
         fin = f"acc / ({t}){R}" if opn == "mean" else "acc"
