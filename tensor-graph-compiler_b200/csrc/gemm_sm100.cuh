@@ -302,14 +302,22 @@ __device__ __forceinline__ void gemm_body(const TgcbArgs& args, const TgcbTmaDes
     for (int tile = blockIdx.x; tile < NUM_TILES; tile += gridDim.x) {
       const int tm = tile / TILES_N;
       const int tn = tile % TILES_N;
+      const long long row0 = (long long)tm * BM + quad * 32;
+      constexpr int CHUNKS = BN / 32;  // 8-column chunks per warp: 64 columns each
+      const int chunk0 = part * CHUNKS;
+      // Side inputs of the first chunk are fetched before waiting for the accumulator,
+      // so their latency overlaps the tensor-core work of this tile.
+      typename Epi::Loads cur[8], nxt[8];
+#pragma unroll
+      for (int it = 0; it < 8; ++it)
+        cur[it] = Epi::load(args, row0 + 4 * it + (lane >> 3), (long long)tn * BN + chunk0 * 8 + (lane & 7));
       bool ok = true;
       if (lane == 0) ok = bar_wait(tfull_bar(acc), acc_phase, abort_flag, args.status, TGCB_STATUS_TIMEOUT_EPILOGUE);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
       tc_fence_after();
-      const long long row0 = (long long)tm * BM + quad * 32;
 #pragma unroll 1
-      for (int chunk = part * (BN / 32); chunk < (part + 1) * (BN / 32); ++chunk) {
+      for (int chunk = chunk0; chunk < chunk0 + CHUNKS; ++chunk) {
         uint32_t r[8];
         tmem_ld8(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + chunk * 8), r);
         // lane = row on the way in; on the way out each lane takes one column of one of four
@@ -319,18 +327,24 @@ __device__ __forceinline__ void gemm_body(const TgcbArgs& args, const TgcbTmaDes
         for (int j = 0; j < 8; ++j) stage[lane * 8 + (j ^ (lane >> 2))] = r[j];
         __syncwarp();
         const long long col0 = (long long)tn * BN + chunk * 8;
+        if (chunk + 1 < chunk0 + CHUNKS) {
+#pragma unroll
+          for (int it = 0; it < 8; ++it) nxt[it] = Epi::load(args, row0 + 4 * it + (lane >> 3), col0 + 8 + (lane & 7));
+        }
 #pragma unroll
         for (int it = 0; it < 8; ++it) {
           const int rr = 4 * it + (lane >> 3);
           const int cc = lane & 7;
           const uint32_t bits = stage[rr * 8 + (cc ^ it)];
           if constexpr (INT8) {
-            Epi::apply(args, row0 + rr, col0 + cc, (int)bits);
+            Epi::apply(args, row0 + rr, col0 + cc, (int)bits, cur[it]);
           } else {
-            Epi::apply(args, row0 + rr, col0 + cc, __uint_as_float(bits));
+            Epi::apply(args, row0 + rr, col0 + cc, __uint_as_float(bits), cur[it]);
           }
         }
         __syncwarp();
+#pragma unroll
+        for (int it = 0; it < 8; ++it) cur[it] = nxt[it];
       }
       tc_fence_before();
       __syncwarp();

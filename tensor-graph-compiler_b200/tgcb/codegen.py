@@ -35,6 +35,7 @@ checked within a tolerance.
 from __future__ import annotations
 
 import math
+import re
 from dataclasses import dataclass, field
 
 from tgcb import ir
@@ -42,6 +43,8 @@ from tgcb.errors import CodegenError
 from tgcb.expr import ExprBuilder, _broadcast_index, ctype, delinearise
 
 NUM_SMS = 148
+_LOAD_LINE = re.compile(r"^\s*const (.+?) (ld_\d+) = (.*);$")
+_LOAD_NAME = re.compile(r"\b(ld_\d+)\b")
 GEMM_THREADS = 576  # tgcb_gemm::THREADS: TMA warp, MMA warp, 16 epilogue warps
 
 # Placeholder for the base pointer of a materialised value; replaced once the plan exists.
@@ -128,6 +131,10 @@ class Lowering:
         self.steps: list[Step] = []
         self.scratch: dict[str, int] = {}  # scratch slot name -> bytes
         self.kernel_count = 0
+        self.request_pos: dict[str, int] = {}  # soft value written to memory -> emitting step
+        self._gen_pos = 0
+        self._step_reads: set[str] = set()
+        self._frontier_memo: dict = {}
 
     # ------------------------------------------------------------------ classification
 
@@ -349,38 +356,56 @@ class Lowering:
             else:
                 owned.setdefault(owner, []).append(r)
 
-        # 3. which hard values are read by a kernel other than their producer
-        def note_reads(names_for_kernel: list[str], own: set[str]):
-            for n in names_for_kernel:
-                for d in self.hard_deps(n):
-                    if d not in own and d not in self.inputs:
+        # 3. emission order: map steps right after the step they depend on. A request
+        #    written by an earlier step is read from memory by later steps (never recomputed),
+        #    so everything below walks expressions only down to that frontier.
+        seq: list[tuple] = [("map", [r]) for r in maps.get(-1, [])]
+        for k, (kind, obj) in enumerate(self.raw):
+            seq.append((kind, obj, owned.get(k, [])))
+            seq.extend(("map", [r]) for r in maps.get(k, []))
+        self.request_pos = {}
+        for pos, item in enumerate(seq):
+            for r in (item[1] if item[0] == "map" else item[2]):
+                self.request_pos[r] = pos
+        self._frontier_memo = {}
+
+        # 4. which hard values are read by a kernel other than their producer
+        def note_reads(roots: list[str], own: set[str], pos: int):
+            for n in roots:
+                for d in self.frontier(n, pos):
+                    if d not in own and d not in self.inputs and self.is_hard(d):
                         self.materialised.add(d)
 
-        for k, (kind, obj) in enumerate(self.raw):
-            if kind == "gemm":
-                note_reads(owned.get(k, []), {obj.name})
+        for pos, item in enumerate(seq):
+            kind = item[0]
+            if kind == "map":
+                note_reads(item[1], set(), pos)
+            elif kind == "gemm":
+                note_reads(item[2], {item[1].name}, pos)
             elif kind == "row":
-                members = set(obj.members)
-                note_reads([self.producers[m].inputs[0] for m in obj.members], members)
-                note_reads(owned.get(k, []), members)
+                members = set(item[1].members)
+                note_reads([self.producers[m].inputs[0] for m in item[1].members], members, pos)
+                note_reads(item[2], members, pos)
             else:
-                note_reads([obj.inputs[0]], set())
-        for k, rs in maps.items():
-            note_reads(rs, set())
+                note_reads([item[1].inputs[0]], set(), pos)
 
-        # 4. emit steps in order, map steps right after the step they depend on
+        # 5. generate the steps in order
         steps: list[Step] = []
-        for r in maps.get(-1, []):
-            steps.append(self._map_step([r]))
-        for k, (kind, obj) in enumerate(self.raw):
-            if kind == "gemm":
-                steps.append(self._gemm_step(obj, owned.get(k, [])))
+        for pos, item in enumerate(seq):
+            self._gen_pos = pos
+            self._step_reads = set()
+            kind = item[0]
+            if kind == "map":
+                new = [self._map_step(item[1])]
+            elif kind == "gemm":
+                new = [self._gemm_step(item[1], item[2])]
             elif kind == "row":
-                steps.append(self._row_step(obj, owned.get(k, [])))
+                new = [self._row_step(item[1], item[2])]
             else:
-                steps.extend(self._reduction_steps(obj))
-            for r in maps.get(k, []):
-                steps.append(self._map_step([r]))
+                new = self._reduction_steps(item[1])
+            for st in new:
+                st.reads = sorted(set(st.reads) | self._step_reads)
+            steps.extend(new)
         self.steps = steps
         return steps
 
@@ -444,9 +469,27 @@ class Lowering:
         return f"tgcb_{stem}_{self.kernel_count}"
 
     def _pointer_of(self, name: str) -> str | None:
-        if name in self.inputs or name in self.materialised:
+        """Base pointer of ``name`` if the kernel being generated reads it from memory."""
+        if name in self.inputs or name in self.materialised or self.request_pos.get(name, 1 << 30) < self._gen_pos:
+            self._step_reads.add(name)
             return PTR(name)
         return None
+
+    def frontier(self, name: str, pos: int) -> frozenset[str]:
+        """Memory-resident values an expression for ``name`` reads when generated at step ``pos``:
+        hard values, and requests materialised by an earlier step."""
+        key = (name, pos)
+        if key in self._frontier_memo:
+            return self._frontier_memo[key]
+        if self.is_hard(name) or self.request_pos.get(name, 1 << 30) < pos:
+            out = frozenset([name])
+        else:
+            acc: set[str] = set()
+            for i in self.producers[name].inputs:
+                acc |= self.frontier(i, pos)
+            out = frozenset(acc)
+        self._frontier_memo[key] = out
+        return out
 
     def _map_step(self, names: list[str]) -> Step:
         out_sizes = self.sizes(names[0])
@@ -612,14 +655,6 @@ class Lowering:
             + "\n  }\n}\n"
         )
         writes = [m for m in members if m in self.materialised] + list(requests)
-        for m in members:
-            for d in self.hard_deps(self.producers[m].inputs[0]):
-                if d not in members_set:
-                    reads.add(d)
-        for r in requests:
-            for d in self.hard_deps(r):
-                if d not in members_set:
-                    reads.add(d)
         return Step(
             "row",
             ",".join(members),
@@ -695,7 +730,7 @@ class Lowering:
             f"  for (int p = 0; p < {P}; ++p) {{ const {t} v = part[p * {C}LL + c]; {self._acc_update(opn, 'acc', 'v', t)} }}\n"
             f"  reinterpret_cast<{t}*>({PTR(name)})[c] = {fin};\n}}\n"
         )
-        reads = sorted(d for d in self.hard_deps(src) if d != name)
+        reads: list[str] = []  # recorded by _pointer_of while generating
         self.materialised.add(name)
         return [
             Step(
@@ -752,7 +787,7 @@ class Lowering:
             f"  acc = {fn}<{t}, {T // 32}>(acc, reinterpret_cast<{t}*>(red_smem));\n"
             f"  if (threadIdx.x == 0) reinterpret_cast<{t}*>({PTR(name)})[0] = {fin};\n}}\n"
         )
-        reads = sorted(d for d in self.hard_deps(src) if d != name)
+        reads: list[str] = []  # recorded by _pointer_of while generating
         self.materialised.add(name)
         return [
             Step(
@@ -806,7 +841,7 @@ class Lowering:
         return Step(
             "reduce",
             name,
-            reads=sorted(d for d in self.hard_deps(src) if d != name),
+            reads=[],
             writes=[name],
             source=src_code,
             launches=[Launch(kname, ((out_n + 255) // 256, 1, 1), (256, 1, 1))],
@@ -848,17 +883,36 @@ class Lowering:
         for r in stores:
             v = eb.value(r, ("row", "col"))
             st.append(f"    reinterpret_cast<{ctype(self.values[r].dtype)}*>({PTR(r)})[row * {N}LL + col] = {v};")
+        # Side-input loads never depend on the accumulator: they go into load(), which the
+        # kernel issues ahead of time (before waiting for the tile, and one chunk ahead while
+        # the previous chunk computes); apply() does the arithmetic and the stores.
+        loads, comps = [], []
+        for line in eb.lines:
+            m = _LOAD_LINE.match(line)
+            # only full-matrix side inputs are worth registers ahead of time; row/column
+            # vectors (biases, scales) are L1 hits and stay inline
+            if m and "row" in m.group(3) and "col" in m.group(3):
+                loads.append(m.groups())
+            else:
+                comps.append(line)
+        members = "".join(f"    {t} {n};\n" for t, n, _ in loads) or "    int unused;\n"
+        load_body = "".join(f"      L.{n} = {e};\n" for t, n, e in loads)
+        fetched = {n for _, n, _ in loads}
+        comp_body = "\n".join(
+            _LOAD_NAME.sub(lambda m: f"L.{m.group(1)}" if m.group(1) in fetched else m.group(1), ln) for ln in comps + st
+        )
         epi_name = f"Epi_{kname}"
         epi = (
             f"struct {epi_name} {{\n"
-            f"  static __device__ __forceinline__ void apply(const TgcbArgs& args, long long row, long long col, const {acc_t} acc) {{\n"
-            f"    if (row >= {M}LL || col >= {N}LL) return;\n" + "\n".join(eb.lines + st) + "\n  }\n};\n"
+            f"  struct Loads {{\n{members}  }};\n"
+            f"  static __device__ __forceinline__ Loads load(const TgcbArgs& args, long long row, long long col) {{\n"
+            f"    Loads L;\n"
+            f"    if (row < {M}LL && col < {N}LL) {{\n{load_body}    }}\n"
+            f"    return L;\n  }}\n"
+            f"  static __device__ __forceinline__ void apply(const TgcbArgs& args, long long row, long long col, const {acc_t} acc, const Loads& L) {{\n"
+            f"    if (row >= {M}LL || col >= {N}LL) return;\n" + comp_body + "\n  }\n};\n"
         )
-        reads = {a_base, b_base}
-        for r in requests:
-            for d in self.hard_deps(r):
-                if d != name:
-                    reads.add(d)
+        reads = {a_base, b_base}  # plus whatever the epilogue loads (recorded by _pointer_of)
         tma_ok = all((op.cols * op.elem_bytes) % 16 == 0 for op in (opa, opb))
         if tma_ok:
             kernel = (
@@ -914,7 +968,7 @@ class Lowering:
             f"    for (int j = 0; j < 16; ++j) {{\n"
             f"      if (col0 + j < {N}LL) {{ const {at} b = {load_b}; {fma} }}\n"
             f"    }}\n  }}\n"
-            f"  for (int j = 0; j < 16; ++j) {epi_name}::apply(args, row, col0 + j, acc[j]);\n}}\n"
+            f"  for (int j = 0; j < 16; ++j) {epi_name}::apply(args, row, col0 + j, acc[j], {epi_name}::load(args, row, col0 + j));\n}}\n"
         )
 
 
