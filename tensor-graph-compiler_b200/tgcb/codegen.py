@@ -100,11 +100,17 @@ def _next_pow2(x: int) -> int:
     return 1 << max(0, (x - 1).bit_length())
 
 
-def row_threads(cols: int) -> int:
+def row_threads(cols: int, rows: int | None = None) -> int:
     """Threads per row in a row kernel: a power of two in [32, 256] giving each thread at most
     32 columns (a single warp per row up to 1024 columns), so a thread keeps up to 32
-    independent loads in flight and reductions of short rows need no block barrier."""
-    return max(32, min(256, _next_pow2(max(1, (cols + 31) // 32))))
+    independent loads in flight and reductions of short rows need no block barrier. When there
+    are too few rows to give every SM 32 warps, rows get more threads (down to 8 columns per
+    thread) so the work spreads evenly over the GPU."""
+    t = max(32, min(256, _next_pow2(max(1, (cols + 31) // 32))))
+    if rows is not None:
+        while t < 256 and rows * (t // 32) < NUM_SMS * 32 and cols >= 16 * t:
+            t *= 2
+    return t
 
 
 ROW_BLOCK = 256  # threads per CTA of a row kernel; 256 // T rows are processed side by side
@@ -533,7 +539,7 @@ class Lowering:
         ss = tuple(group.src_sizes)
         C = ss[-1]
         R = _prod(ss[:-1])
-        T = row_threads(C)
+        T = row_threads(C, R)
         W = T // 32
         npt = (C + T - 1) // T
         unrolled = npt <= 32

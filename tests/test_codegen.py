@@ -63,6 +63,12 @@ def test_row_threads(cols, expect):
     assert row_threads(cols) == expect
 
 
+@pytest.mark.parametrize("rows,cols,expect", [(8192, 1024, 32), (4096, 1024, 64), (64, 1024, 128), (64, 256, 32), (4, 70, 32)])
+def test_row_threads_spread_few_rows(rows, cols, expect):
+    """Few rows get more threads each (never below 8 columns per thread)."""
+    assert row_threads(cols, rows) == expect
+
+
 def test_plans_keep_live_values_apart():
     for g in (workloads.mlp_graph(ir.Builder, rows=512), load_graph("train_grad_small"), load_graph("fixture_softmax_graph")):
         og, order, plan, mod, low = runtime.generate(g)

@@ -73,7 +73,7 @@ def test_row_reductions_bit_exact_to_declared_bracketing(cuda, rows, cols):
     g = b.finish(b.sum(x, [1]), b.max(x, [1]), b.sum(b.mul(x, x), [1]), b.mean(x, [1], keepdims=True))
     xv = torch.randn(rows, cols, generator=torch.Generator().manual_seed(rows * 7 + cols))
     _, (s, m, ss, mean) = run(g, {"x": xv})
-    T = row_threads(cols)
+    T = row_threads(cols, rows)
     xn = xv.numpy()
     assert np.array_equal(s.numpy(), bracketing.row_tree(xn, T))
     assert np.array_equal(m.numpy(), bracketing.row_tree(xn, T, "max"))
