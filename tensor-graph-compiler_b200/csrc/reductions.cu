@@ -9,6 +9,9 @@
 //     divides n, otherwise a walk of the L halvings), sums it exactly like _pairwise, and
 //     256-node groups are combined as perfect trees in shared memory;
 //   * levels 1..: the same perfect-tree combine over 256 partials at a time, until one.
+//   Where a level is uniform and at least 1024 wide, a block takes 1024 consecutive nodes
+//   instead (4 per thread in registers, xor shuffles across lanes, 8 warp partials last):
+//   the same perfect tree with one barrier per block instead of eight.
 // Every addition is the one _pairwise performs, so the result is bit-identical.
 //
 // Sequential sum (summation.py:56-61) is one dependent chain of n float additions; one
@@ -98,6 +101,91 @@ __global__ void __launch_bounds__(kGroup) pairwise_leaves(const float* __restric
   s[threadIdx.x] = v;
   const int count = (int)(nodes < kGroup ? nodes : kGroup);
   const float r = tree256(s, count);
+  if (threadIdx.x == 0) out[blockIdx.x] = r;
+}
+
+// Fast path for the perfect part of the tree: each thread takes 4 adjacent values (leaves, or
+// partials of a previous level), adds them as ((a+b)+(c+d)), lanes combine by xor shuffles
+// 1,2,4,8,16 (adjacent subtrees first), and the 8 warps by a balanced tree in shared memory:
+// a perfect tree over 1024 consecutive values per block, the same additions as tree256 makes
+// but with one barrier. `count` is a power of two >= 1024.
+constexpr int kFastPer = 4;
+constexpr int kFastSpan = kGroup * kFastPer;
+
+// Balanced tree over the 8 warp partials of a block; `writer` is the one lane per warp that
+// holds its warp's partial. The result is valid on thread 0.
+__device__ __forceinline__ float combine_warps(float v, bool writer, float* s) {
+  if (writer) s[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = 0.0f;
+  if (threadIdx.x == 0) {
+    float w[kGroup / 32];
+#pragma unroll
+    for (int i = 0; i < kGroup / 32; ++i) w[i] = s[i];
+#pragma unroll
+    for (int width = 1; width < kGroup / 32; width *= 2)
+#pragma unroll
+      for (int i = 0; i < kGroup / 32; i += 2 * width) w[i] = __fadd_rn(w[i], w[i + width]);
+    r = w[0];
+  }
+  return r;
+}
+
+__device__ __forceinline__ float fast_block_tree(float v, float* s) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return combine_warps(v, (threadIdx.x & 31) == 0, s);
+}
+
+// 128 leaves of exactly 8 values each (4 KiB from p), read coalesced: in load k the warp reads
+// 512 contiguous bytes, lane i the float4 that is half (i & 1) of leaf 16k + i/2. The even
+// lane's running sum of its 4 values goes to the odd lane, which finishes the leaf's
+// left-to-right chain; xor shuffles 2,4,8,16 build the perfect tree over each load's 16 leaves
+// (odd lanes pair with odd lanes), and a register tree over the 8 loads the warp's 128-leaf
+// subtree. The result is valid on the odd lanes.
+__device__ __forceinline__ float warp_leaves8(const float4* __restrict__ p) {
+  const int lane = threadIdx.x & 31;
+  float4 q[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) q[k] = __ldg(p + k * 32 + lane);
+  float r[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float head = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, q[k].x), q[k].y), q[k].z), q[k].w);
+    const float left = __shfl_xor_sync(0xffffffffu, head, 1);
+    float t = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(left, q[k].x), q[k].y), q[k].z), q[k].w);
+#pragma unroll
+    for (int o = 2; o < 32; o <<= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
+    r[k] = t;
+  }
+  return __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3])),
+                   __fadd_rn(__fadd_rn(r[4], r[5]), __fadd_rn(r[6], r[7])));
+}
+
+__global__ void __launch_bounds__(kGroup) pairwise_leaves_fast(const float* __restrict__ x, long long n, int L,
+                                                               int block, float* __restrict__ out) {
+  __shared__ float s[kGroup / 32];
+  const long long size = n >> L;
+  float r;
+  if (size == 8 && block >= 8 && ((reinterpret_cast<uintptr_t>(x) & 15u) == 0)) {
+    const long long leaf0 = (long long)blockIdx.x * kFastSpan + (threadIdx.x >> 5) * 128;
+    const float w = warp_leaves8(reinterpret_cast<const float4*>(x) + leaf0 * 2);
+    r = combine_warps(w, (threadIdx.x & 31) == 1, s);
+  } else {
+    const long long j0 = ((long long)blockIdx.x * kGroup + threadIdx.x) * kFastPer;
+    float v[kFastPer];
+#pragma unroll
+    for (int g = 0; g < kFastPer; ++g) v[g] = node_value(x, (j0 + g) * size, size, block);
+    r = fast_block_tree(__fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3])), s);
+  }
+  if (threadIdx.x == 0) out[blockIdx.x] = r;
+}
+
+__global__ void __launch_bounds__(kGroup) pairwise_combine_fast(const float* __restrict__ in, float* __restrict__ out) {
+  __shared__ float s[kGroup / 32];
+  const float4 q = __ldg(reinterpret_cast<const float4*>(in) + (long long)blockIdx.x * kGroup + threadIdx.x);
+  const float t4 = __fadd_rn(__fadd_rn(q.x, q.y), __fadd_rn(q.z, q.w));
+  const float r = fast_block_tree(t4, s);
   if (threadIdx.x == 0) out[blockIdx.x] = r;
 }
 
@@ -238,17 +326,27 @@ int tgcb_sum_pairwise_f32(const float* x, uint64_t n, int block, float* out, voi
   const long long nodes = 1ll << L;
   const int uniform = (n % (uint64_t)nodes) == 0 ? 1 : 0;
   float* buf = static_cast<float*>(scratch);
-  long long groups = (nodes + kGroup - 1) / kGroup;
+  // Perfect-tree levels of 1024 values per block where the level is wide enough; the
+  // 256-per-block kernels finish narrow levels and irregular (non-uniform) leaves.
+  const bool fast0 = uniform && nodes >= kFastSpan;
+  long long groups = fast0 ? nodes / kFastSpan : (nodes + kGroup - 1) / kGroup;
   float* dst = groups == 1 ? out : buf;
-  pairwise_leaves<<<(unsigned)groups, kGroup, 0, s>>>(x, (long long)n, L, block, uniform, dst);
+  if (fast0)
+    pairwise_leaves_fast<<<(unsigned)groups, kGroup, 0, s>>>(x, (long long)n, L, block, dst);
+  else
+    pairwise_leaves<<<(unsigned)groups, kGroup, 0, s>>>(x, (long long)n, L, block, uniform, dst);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return report(TGCB_E_CUDA, "pairwise_leaves", e);
   float* src = buf;
   float* next = buf + groups;
   while (groups > 1) {
-    const long long g2 = (groups + kGroup - 1) / kGroup;
+    const bool fast = groups >= kFastSpan && groups % kFastSpan == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
+    const long long g2 = fast ? groups / kFastSpan : (groups + kGroup - 1) / kGroup;
     float* d = g2 == 1 ? out : next;
-    pairwise_combine<<<(unsigned)g2, kGroup, 0, s>>>(src, groups, d);
+    if (fast)
+      pairwise_combine_fast<<<(unsigned)g2, kGroup, 0, s>>>(src, d);
+    else
+      pairwise_combine<<<(unsigned)g2, kGroup, 0, s>>>(src, groups, d);
     e = cudaGetLastError();
     if (e != cudaSuccess) return report(TGCB_E_CUDA, "pairwise_combine", e);
     src = next;

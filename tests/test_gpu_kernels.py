@@ -54,7 +54,9 @@ def test_summation_vectors_bit_exact_to_tgc(cuda, summ):
         assert summation.pairwise(v, block=3) == vec["pairwise_block_3"]
 
 
-@pytest.mark.parametrize("n", [1, 2, 7, 8, 9, 17, 255, 256, 257, 1000, 12345, 65537, 1000003, (1 << 21) + 3])
+@pytest.mark.parametrize(
+    "n", [1, 2, 7, 8, 9, 17, 255, 256, 257, 1000, 4096, 12345, 65537, 196608, 1000003, (1 << 21) + 3, 3 << 20, 1 << 22]
+)
 @pytest.mark.parametrize("block", [1, 3, 8, 16])
 def test_pairwise_any_length_any_block(cuda, n, block):
     v = torch.rand(n, generator=torch.Generator().manual_seed(n + block)) - 0.3
@@ -67,8 +69,9 @@ def test_sequential_any_length(cuda, n):
     assert summation.sequential(v.cuda()) == bracketing.sequential(v.numpy())
 
 
-def test_pairwise_on_an_unaligned_view(cuda):
-    v = torch.rand(4099, generator=torch.Generator().manual_seed(1))
+@pytest.mark.parametrize("n", [4099, (1 << 20) + 3])
+def test_pairwise_on_an_unaligned_view(cuda, n):
+    v = torch.rand(n, generator=torch.Generator().manual_seed(1))
     vc = v.cuda()[3:]
     assert summation.pairwise(vc) == bracketing.pairwise(v.numpy()[3:])
 
