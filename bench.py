@@ -163,6 +163,91 @@ class ClockSampler:
         }
 
 
+class NvmlClockSampler:
+    """NVML read every millisecond in a thread (read-only queries of the SM clock, its maximum,
+    power and the active clock-event reasons); summarises the samples of the timed region.
+
+    The timed regions here last milliseconds, well under nvidia-smi's shortest period, so the
+    same readings nvidia-smi reports are taken directly from NVML for the GPU this rank drives
+    (matched by UUID). Falls back to ``ClockSampler`` when NVML is unavailable.
+    """
+
+    def __init__(self, local: int):
+        self.local = local
+        self.samples: list[tuple[float, float, float, float, int]] = []
+        self.t0 = self.t1 = None
+        self.stop_flag = threading.Event()
+
+    def start(self) -> bool:
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(self.local).uuid)
+            try:
+                h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except pynvml.NVMLError:
+                h = pynvml.nvmlDeviceGetHandleByIndex(self.local)
+            self.nvml, self.h = pynvml, h
+            self.max_sm = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        except Exception:  # noqa: BLE001 - any NVML failure means: use nvidia-smi instead
+            return False
+
+        def poll():
+            p = self.nvml
+            while not self.stop_flag.is_set():
+                try:
+                    self.samples.append((
+                        time.time(),
+                        float(p.nvmlDeviceGetClockInfo(self.h, p.NVML_CLOCK_SM)),
+                        self.max_sm,
+                        p.nvmlDeviceGetPowerUsage(self.h) / 1000.0,
+                        int(p.nvmlDeviceGetCurrentClocksEventReasons(self.h)),
+                    ))
+                except p.NVMLError:
+                    pass
+                time.sleep(0.001)
+
+        self.thread = threading.Thread(target=poll, daemon=True)
+        self.thread.start()
+        return True
+
+    def mark_start(self) -> None:
+        self.t0 = time.time()
+
+    def mark_end(self) -> None:
+        self.t1 = time.time()
+
+    def stop(self) -> dict:
+        time.sleep(0.01)
+        self.stop_flag.set()
+        self.thread.join(timeout=5)
+        p = self.nvml
+        t0, t1 = self.t0 or 0.0, self.t1 or time.time()
+        inside = [x for x in self.samples if t0 <= x[0] <= t1]
+        use = inside or ([x for x in self.samples if x[0] < t0][-1:] + [x for x in self.samples if x[0] > t1][:1])
+        if not use:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "source": "nvml"}
+        bits = {
+            "hw_slowdown": p.nvmlClocksEventReasonHwSlowdown,
+            "hw_thermal_slowdown": p.nvmlClocksEventReasonHwThermalSlowdown,
+            "sw_thermal_slowdown": p.nvmlClocksEventReasonSwThermalSlowdown,
+            "sw_power_cap": p.nvmlClocksEventReasonSwPowerCap,
+        }
+        reasons = sorted({name for x in use for name, b in bits.items() if x[4] & b})
+        return {
+            "sm_mhz": statistics.median(x[1] for x in use),
+            "sm_max_mhz": max(x[2] for x in use),
+            "sm_mhz_min": min(x[1] for x in use),
+            "power_w_max": round(max(x[3] for x in use), 1),
+            "samples": len(use),
+            "samples_inside_timed_region": len(inside),
+            "reasons": reasons,
+            "source": "nvml, 1 ms period",
+        }
+
+
 # ----------------------------------------------------------------------------- workloads
 
 
@@ -325,7 +410,14 @@ class Int8Workload(GraphWorkload):
 
 
 class LongSumWorkload:
-    """Pairwise (block 8) float32 sum of 2^26 values, bit-exact to tgc's summation.pairwise."""
+    """Pairwise (block 8) float32 sum of 2^26 values per GPU, bit-exact to tgc's summation.pairwise.
+
+    On N GPUs the vector is N * 2^26 values long and each rank holds one depth-log2(N) subtree
+    of the halving; a step sums the rank's slice with the same kernels, all-gathers the N
+    partials (one float each, NCCL) and combines them by the perfect tree of the top levels, so
+    every rank ends with the whole vector's bit-exact sum. Work per GPU is fixed ("weak"); one
+    unit is 2^26 values summed.
+    """
 
     name = "longsum"
     unit = "sums/s"
@@ -334,16 +426,25 @@ class LongSumWorkload:
 
     def __init__(self, rank: int):
         self.rank = rank
+        self.world = 1
 
     def config(self):
-        return {"workload": "pairwise (block 8) sum of 2^26 fp32 values ~U(0,1) with one 1e8 entry",
+        return {"workload": "pairwise (block 8) sum of 2^26 fp32 values ~U(0,1) with one 1e8 entry per GPU; "
+                            "on N GPUs one sum of the N * 2^26-value vector per step",
                 "bytes_per_sum": self.n * 4, "l2": L2_NOTE}
 
-    def setup(self, device):
+    def parallelism(self, n: int) -> str:
+        if n == 1:
+            return "dp1: one 2^26-value sum"
+        return (f"dp{n}: each GPU sums its 2^26-value subtree, NCCL all-gather of {n} partials, "
+                "perfect-tree combine of the top levels on every GPU")
+
+    def setup(self, device, dist=None, world: int = 1):
         import torch
 
         from tgcb import summation, workloads
 
+        self.world = world
         self.v, _ = workloads.longsum_input(self.n, seed=self.rank)
         self.dev = self.v.to(device)
         self.host = self.v.pin_memory()
@@ -351,27 +452,45 @@ class LongSumWorkload:
         self.out_host = torch.empty(1, dtype=torch.float32).pin_memory()
         self.scratch = torch.empty(summation.scratch_bytes(self.n), dtype=torch.uint8, device=device)
         self.staging = torch.empty_like(self.dev)
+        self.sharded = None
+        if world > 1:
+            self.sharded = summation.ShardedPairwise(self.n * world, self.rank, world, dist, device)
+            self.partial = torch.empty(1, dtype=torch.float32, device=device)
 
     def launches_per_step(self) -> int:
-        return 3  # leaves, then two combine levels for 2^23 nodes
+        # leaves, then two combine levels for 2^23 nodes; on N GPUs also the top-level tree
+        # (the all-gather is NCCL's kernel, not counted)
+        return 3 if self.world == 1 else 4
 
     def step_profiled(self) -> list[float]:
         import torch
 
         from tgcb import summation
 
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        summation.pairwise_into(self.dev, self.out, self.scratch)
-        e.record()
-        e.synchronize()
-        return [s.elapsed_time(e)]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        if self.sharded is None:
+            ev[0].record()
+            summation.pairwise_into(self.dev, self.out, self.scratch)
+            ev[1].record()
+            ev[1].synchronize()
+            return [ev[0].elapsed_time(ev[1])]
+        ev[0].record()
+        summation.pairwise_into(self.dev, self.sharded.partial, self.scratch)
+        ev[1].record()
+        self.sharded.dist.all_gather_into_tensor(self.sharded.gathered, self.sharded.partial)
+        summation.perfect_tree_into(self.sharded.gathered, self.out)
+        ev[2].record()
+        ev[2].synchronize()
+        return [ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])]
 
     def step_e2e(self) -> None:
         from tgcb import summation
 
         self.staging.copy_(self.host, non_blocking=True)
-        summation.pairwise_into(self.staging, self.out, self.scratch)
+        if self.sharded is None:
+            summation.pairwise_into(self.staging, self.out, self.scratch)
+        else:
+            self.sharded.into(self.staging, self.out)
         self.out_host.copy_(self.out, non_blocking=True)
 
     def h2d_bytes(self) -> int:
@@ -381,7 +500,10 @@ class LongSumWorkload:
         return 4
 
     def kernel_work(self) -> list[dict]:
-        return [{"name": "pairwise_leaves+pairwise_combine", "kind": "longsum", "bound": "hbm", "work": self.n * 4}]
+        work = [{"name": "pairwise_leaves+pairwise_combine", "kind": "longsum", "bound": "hbm", "work": self.n * 4}]
+        if self.world > 1:
+            work.append({"name": "nccl_all_gather+perfect_tree", "kind": "exchange", "bound": "nvlink", "work": 4 * self.world})
+        return work
 
     def cpu_program(self):
         from oracle import bracketing
@@ -586,6 +708,8 @@ def _main(json_out) -> int:
     if args.workload == "train":
         wl.global_rows = args.train_rows
         wl.setup(device, dist, n)
+    elif args.workload == "longsum":
+        wl.setup(device, dist, n)
     else:
         wl.setup(device)
     scaling = getattr(wl, "scaling", "weak")
@@ -600,8 +724,10 @@ def _main(json_out) -> int:
 
     from tgcb.runtime import delay
 
-    sampler = ClockSampler(local)
-    sampler.start()
+    sampler = NvmlClockSampler(local)
+    if not sampler.start():
+        sampler = ClockSampler(local)
+        sampler.start()
     warm = max(args.warmup, 3)
     for _ in range(warm):
         wl.step_profiled()
@@ -690,7 +816,7 @@ def _main(json_out) -> int:
             "vs_baseline": None,
             "dtype": wl.dtype,
             "data": "synthetic: seeded torch.randn inputs and random-init weights of the workload's shapes",
-            "config": {**wl.config(), "parallelism": f"dp{n}: " + (
+            "config": {**wl.config(), "parallelism": wl.parallelism(n) if hasattr(wl, "parallelism") else f"dp{n}: " + (
                 f"{wl.global_rows // n} rows per GPU, gradients averaged by NCCL all-reduce overlapped with the backward"
                 if args.workload == "train" else "independent row shards per GPU, no collective")},
             "roofline": {

@@ -143,6 +143,13 @@ size_t tgcb_sum_pairwise_scratch_bytes(uint64_t n, int block);
 int tgcb_sum_pairwise_f32(const float* x, uint64_t n, int block, float* out, void* scratch, size_t scratch_bytes,
                           void* stream);
 
+/* The top levels of a pairwise sum split across GPUs: a perfect binary tree over `count`
+ * partials in index order (count a power of two, 1..256): ((p0+p1)+(p2+p3))+... . When each
+ * of 2^k GPUs holds one depth-k node of tgc's _pairwise halving (tgc/analysis/summation.py:
+ * 77-85) and has summed it with tgcb_sum_pairwise_f32, the gathered partials combined here give
+ * the whole vector's _pairwise value bit for bit. Writes *out (device). */
+int tgcb_sum_perfect_tree_f32(const float* partials, uint32_t count, float* out, void* stream);
+
 /* Sequential sum from 0.0f left to right, bit-exact to tgc/analysis/summation.py:56-61. */
 int tgcb_sum_sequential_f32(const float* x, uint64_t n, float* out, void* stream);
 

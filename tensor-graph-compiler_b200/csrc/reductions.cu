@@ -356,6 +356,17 @@ int tgcb_sum_pairwise_f32(const float* x, uint64_t n, int block, float* out, voi
   return TGCB_OK;
 }
 
+int tgcb_sum_perfect_tree_f32(const float* partials, uint32_t count, float* out, void* stream) {
+  if (partials == nullptr || out == nullptr)
+    return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_perfect_tree_f32", "null pointer");
+  if (count == 0 || count > (uint32_t)kGroup || (count & (count - 1)) != 0)
+    return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_perfect_tree_f32", "count must be a power of two from 1 to 256");
+  pairwise_combine<<<1, kGroup, 0, static_cast<cudaStream_t>(stream)>>>(partials, (long long)count, out);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return report(TGCB_E_CUDA, "pairwise_combine", e);
+  return TGCB_OK;
+}
+
 int tgcb_sum_sequential_f32(const float* x, uint64_t n, float* out, void* stream) {
   if (x == nullptr || out == nullptr) return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_sequential_f32", "null pointer");
   if (n == 0) return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_sequential_f32", "there is nothing to sum");

@@ -5,6 +5,12 @@ float tgc's functions return for the same values (summation.py:56-85), computed 
 library's kernels (tgcb_sum_pairwise_f32, tgcb_sum_sequential_f32). The input checks and
 their ``ConfigError`` messages follow tgc's ``_checked`` (summation.py:36-44).
 ``*_into`` variants write the result to a device scalar on a stream without synchronising.
+
+Across GPUs the pairwise order shards without losing bit-exactness: for 2^k ranks each rank
+holds one depth-k node of the halving (``shard_ranges``), sums it with the same kernels (a node's
+_pairwise value depends only on its own values), and the 2^k partials, gathered in rank order,
+are the leaves of the perfect tree that forms the top k levels (``tgcb_sum_perfect_tree_f32``).
+``ShardedPairwise`` does that with one all-gather of one float per rank.
 """
 
 from __future__ import annotations
@@ -56,6 +62,103 @@ def sequential_into(values: torch.Tensor, out: torch.Tensor, stream=None) -> Non
         ctypes.c_void_p(v.data_ptr()), v.numel(), ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(s.cuda_stream)
     )
     _lib.check(rc, "tgcb_sum_sequential_f32")
+
+
+def levels_for(n: int, block: int = DEFAULT_BLOCK) -> int:
+    """Depth L of the perfect part of _pairwise's tree: the least L with n >> L <= block."""
+    if n < 1 or block < 1:
+        raise ConfigError(f"no pairwise tree over {n} values with blocks of {block}")
+    levels = 0
+    while (n >> levels) > block:
+        levels += 1
+    return levels
+
+
+def subtree_range(n: int, depth: int, index: int) -> tuple[int, int]:
+    """[start, stop) of node ``index`` at ``depth`` of _pairwise's halving of n values.
+
+    A range of size s splits into its first s // 2 values and the rest (summation.py:81-84);
+    bit ``depth-1-level`` of ``index`` says which half is taken at each level.
+    """
+    if not 0 <= index < (1 << depth):
+        raise ConfigError(f"node {index} is outside depth {depth}")
+    start, size = 0, n
+    for level in range(depth - 1, -1, -1):
+        half = size // 2
+        if (index >> level) & 1:
+            start, size = start + half, size - half
+        else:
+            size = half
+    return start, start + size
+
+
+def shard_ranges(n: int, shards: int, block: int = DEFAULT_BLOCK) -> list[tuple[int, int]]:
+    """The contiguous ranges 2^k shards take so that their pairwise sums are depth-k nodes.
+
+    Refuses a shard count that is not a power of two, or one deeper than the perfect part of
+    the tree (a node there would be a leaf block, summed sequentially, not split).
+    """
+    if shards < 1 or shards & (shards - 1):
+        raise ConfigError(f"the pairwise tree shards over a power of two, not {shards}")
+    depth = shards.bit_length() - 1
+    if shards > 1 and depth > levels_for(n, block):
+        raise ConfigError(f"{n} values in blocks of {block} do not split {shards} ways inside the tree")
+    if shards > 256:
+        raise ConfigError("at most 256 shards are combined")
+    return [subtree_range(n, depth, j) for j in range(shards)]
+
+
+def perfect_tree_into(partials: torch.Tensor, out: torch.Tensor, stream=None) -> None:
+    """((p0+p1)+(p2+p3))+... over a power-of-two count of float32 partials, on the GPU."""
+    p = _checked(partials)
+    if p.numel() > 256 or p.numel() & (p.numel() - 1):
+        raise ConfigError(f"a perfect tree takes a power of two from 1 to 256 partials, not {p.numel()}")
+    _lib.ensure_device(p.device.index)
+    s = stream if stream is not None else torch.cuda.current_stream(p.device)
+    rc = _lib.load().tgcb_sum_perfect_tree_f32(
+        ctypes.c_void_p(p.data_ptr()), p.numel(), ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(s.cuda_stream)
+    )
+    _lib.check(rc, "tgcb_sum_perfect_tree_f32")
+
+
+class ShardedPairwise:
+    """The pairwise sum of an n-value vector whose ``shard_ranges`` slices live one per rank.
+
+    ``dist`` is ``torch.distributed`` (NCCL on GPUs); every rank calls ``into`` (or ``__call__``)
+    with its own slice and gets the whole vector's sum, bit-exact to tgc's ``pairwise``.
+    """
+
+    def __init__(self, n: int, rank: int, world: int, dist, device, block: int = DEFAULT_BLOCK, *,
+                 shard_sum=None, tree=None):
+        """``shard_sum(local, out)`` and ``tree(partials, out)`` default to the library's kernels;
+        tests on CPU ranks pass the oracle's orders instead."""
+        self.ranges = shard_ranges(n, world, block)
+        self.n, self.rank, self.world, self.dist, self.block = n, rank, world, dist, block
+        start, stop = self.ranges[rank]
+        self.local = stop - start
+        self.partial = torch.empty(1, dtype=torch.float32, device=device)
+        self.gathered = torch.empty(world, dtype=torch.float32, device=device)
+        if shard_sum is None:
+            scratch = torch.empty(max(1, scratch_bytes(self.local, block)), dtype=torch.uint8, device=device)
+            shard_sum = lambda local, out: pairwise_into(local, out, scratch, block)  # noqa: E731
+        self._shard_sum = shard_sum
+        self._tree = tree if tree is not None else perfect_tree_into
+
+    def into(self, local: torch.Tensor, out: torch.Tensor) -> None:
+        """Writes the whole vector's sum to ``out`` (one float32) on every rank."""
+        if local.numel() != self.local:
+            raise ConfigError(f"rank {self.rank} holds {self.local} of the {self.n} values, got {local.numel()}")
+        self._shard_sum(local, self.partial)
+        if self.world == 1:
+            out.copy_(self.partial)
+            return
+        self.dist.all_gather_into_tensor(self.gathered, self.partial)
+        self._tree(self.gathered, out)
+
+    def __call__(self, local: torch.Tensor) -> float:
+        out = torch.empty(1, dtype=torch.float32, device=local.device)
+        self.into(local, out)
+        return float(out.item())
 
 
 def pairwise(values: torch.Tensor, block: int = DEFAULT_BLOCK) -> float:

@@ -41,6 +41,42 @@ def test_long_sum_bit_exact_to_tgc(cuda, summ):
     assert abs(p - exact) / exact < abs(s - exact) / exact
 
 
+@pytest.mark.parametrize("shards", [2, 4, 8])
+def test_long_sum_in_shards_bit_exact_to_tgc(cuda, summ, shards):
+    """The 2^26 sum split into depth-k subtrees (one per rank), each summed by the kernels and
+    the partials combined by tgcb_sum_perfect_tree_f32: tgc's pairwise value, bit for bit."""
+    v, _ = workloads.longsum_input()
+    vc = v.cuda()
+    parts = torch.empty(shards, dtype=torch.float32, device="cuda")
+    for j, (a, b) in enumerate(summation.shard_ranges(v.numel(), shards)):
+        scratch = torch.empty(summation.scratch_bytes(b - a), dtype=torch.uint8, device="cuda")
+        summation.pairwise_into(vc[a:b], parts[j:j + 1], scratch)
+    out = torch.empty(1, dtype=torch.float32, device="cuda")
+    summation.perfect_tree_into(parts, out)
+    assert float(out.item()) == summ["longsum"]["pairwise"]
+
+
+@pytest.mark.parametrize("count", [1, 2, 8, 64, 256])
+def test_perfect_tree(cuda, count):
+    p = torch.rand(count, generator=torch.Generator().manual_seed(count)) * 1e4 - 3e3
+    out = torch.empty(1, dtype=torch.float32, device="cuda")
+    summation.perfect_tree_into(p.cuda(), out)
+    want = [np.float32(x) for x in p.numpy()]
+    while len(want) > 1:
+        want = [np.float32(want[i] + want[i + 1]) for i in range(0, len(want), 2)]
+    assert float(out.item()) == float(want[0])
+
+
+@pytest.mark.parametrize("count", [3, 512])
+def test_perfect_tree_refuses(cuda, count):
+    out = torch.empty(1, dtype=torch.float32, device="cuda")
+    ones = torch.ones(count, device="cuda")
+    with pytest.raises(ConfigError):
+        summation.perfect_tree_into(ones, out)
+    rc = _lib.load().tgcb_sum_perfect_tree_f32(ctypes.c_void_p(ones.data_ptr()), count, ctypes.c_void_p(out.data_ptr()), None)
+    assert rc == _lib.TGCB_E_INVALID and "power of two" in _lib.last_error()
+
+
 def test_summation_vectors_bit_exact_to_tgc(cuda, summ):
     gens = {
         "uniform": lambda c, s: np.asarray(np.random.default_rng(s).uniform(0.5, 1.5, size=c), dtype=np.float32),

@@ -74,3 +74,39 @@ def test_two_nccl_ranks_match_the_whole_batch(tmp_path):
     for a, b, r in zip(r0, r1, ref, strict=True):
         assert torch.equal(a, b)
         assert rel_err(a, r) < TF32_TOL
+
+
+def _nccl_sum_rank(rank: int, world: int, port: int, out_dir: str) -> None:
+    import datetime
+
+    import torch.distributed as dist
+
+    from tgcb import summation
+
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "NCCL_NVLS_ENABLE": "0"})
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=datetime.timedelta(seconds=60))
+    try:
+        v, _ = workloads.longsum_input()
+        s = summation.ShardedPairwise(v.numel(), rank, world, dist, dev)
+        a, b = s.ranges[rank]
+        got = s(v[a:b].to(dev))
+        torch.save(torch.tensor([got], dtype=torch.float64), os.path.join(out_dir, f"sum{rank}.pt"))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_nccl_ranks_sum_the_long_vector_bit_exact(tmp_path):
+    import json
+
+    from conftest import GOLDEN
+
+    world = 2
+    mp.start_processes(_nccl_sum_rank, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    with open(os.path.join(GOLDEN, "summation.json")) as f:
+        want = json.load(f)["longsum"]["pairwise"]
+    for r in range(world):
+        assert float(torch.load(os.path.join(tmp_path, f"sum{r}.pt"))[0]) == want
