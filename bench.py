@@ -458,9 +458,9 @@ class LongSumWorkload:
             self.partial = torch.empty(1, dtype=torch.float32, device=device)
 
     def launches_per_step(self) -> int:
-        # leaves, then two combine levels for 2^23 nodes; on N GPUs also the top-level tree
-        # (the all-gather is NCCL's kernel, not counted)
-        return 3 if self.world == 1 else 4
+        # one pairwise_fused launch (after a 4-byte counter reset); on N GPUs also the
+        # top-level tree (the all-gather is NCCL's kernel, not counted)
+        return 1 if self.world == 1 else 2
 
     def step_profiled(self) -> list[float]:
         import torch
@@ -500,7 +500,7 @@ class LongSumWorkload:
         return 4
 
     def kernel_work(self) -> list[dict]:
-        work = [{"name": "pairwise_leaves+pairwise_combine", "kind": "longsum", "bound": "hbm", "work": self.n * 4}]
+        work = [{"name": "pairwise_fused", "kind": "longsum", "bound": "hbm", "work": self.n * 4}]
         if self.world > 1:
             work.append({"name": "nccl_all_gather+perfect_tree", "kind": "exchange", "bound": "nvlink", "work": 4 * self.world})
         return work

@@ -11,7 +11,9 @@
 //   * levels 1..: the same perfect-tree combine over 256 partials at a time, until one.
 //   Where a level is uniform and at least 1024 wide, a block takes 1024 consecutive nodes
 //   instead (4 per thread in registers, xor shuffles across lanes, 8 warp partials last):
-//   the same perfect tree with one barrier per block instead of eight.
+//   the same perfect tree with one barrier per block instead of eight. When that level has
+//   256..16384 blocks the whole sum is one launch: the last block to finish combines every
+//   block's partial (pairwise_fused).
 // Every addition is the one _pairwise performs, so the result is bit-identical.
 //
 // Sequential sum (summation.py:56-61) is one dependent chain of n float additions; one
@@ -162,23 +164,74 @@ __device__ __forceinline__ float warp_leaves8(const float4* __restrict__ p) {
                    __fadd_rn(__fadd_rn(r[4], r[5]), __fadd_rn(r[6], r[7])));
 }
 
-__global__ void __launch_bounds__(kGroup) pairwise_leaves_fast(const float* __restrict__ x, long long n, int L,
-                                                               int block, float* __restrict__ out) {
-  __shared__ float s[kGroup / 32];
+// The 1024 depth-L nodes of this block (uniform leaves), as one perfect-tree value on thread 0.
+__device__ __forceinline__ float leaves_block(const float* __restrict__ x, long long n, int L, int block, float* s) {
   const long long size = n >> L;
-  float r;
   if (size == 8 && block >= 8 && ((reinterpret_cast<uintptr_t>(x) & 15u) == 0)) {
     const long long leaf0 = (long long)blockIdx.x * kFastSpan + (threadIdx.x >> 5) * 128;
     const float w = warp_leaves8(reinterpret_cast<const float4*>(x) + leaf0 * 2);
-    r = combine_warps(w, (threadIdx.x & 31) == 1, s);
-  } else {
-    const long long j0 = ((long long)blockIdx.x * kGroup + threadIdx.x) * kFastPer;
-    float v[kFastPer];
-#pragma unroll
-    for (int g = 0; g < kFastPer; ++g) v[g] = node_value(x, (j0 + g) * size, size, block);
-    r = fast_block_tree(__fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3])), s);
+    return combine_warps(w, (threadIdx.x & 31) == 1, s);
   }
+  const long long j0 = ((long long)blockIdx.x * kGroup + threadIdx.x) * kFastPer;
+  float v[kFastPer];
+#pragma unroll
+  for (int g = 0; g < kFastPer; ++g) v[g] = node_value(x, (j0 + g) * size, size, block);
+  return fast_block_tree(__fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3])), s);
+}
+
+__global__ void __launch_bounds__(kGroup) pairwise_leaves_fast(const float* __restrict__ x, long long n, int L,
+                                                               int block, float* __restrict__ out) {
+  __shared__ float s[kGroup / 32];
+  const float r = leaves_block(x, n, L, block, s);
   if (threadIdx.x == 0) out[blockIdx.x] = r;
+}
+
+// Perfect tree over C consecutive partials that other blocks of this launch wrote: loads go
+// through L2 (ld.global.cg), never the non-coherent read-only path.
+template <int C>
+__device__ __forceinline__ float chunk_tree(const float* p) {
+  float v[C];
+#pragma unroll
+  for (int i = 0; i < C; ++i) v[i] = __ldcg(p + i);
+#pragma unroll
+  for (int w = 1; w < C; w *= 2)
+#pragma unroll
+    for (int i = 0; i < C; i += 2 * w) v[i] = __fadd_rn(v[i], v[i + w]);
+  return v[0];
+}
+
+// Whole sum in one launch when the leaf level has 256 to 16384 blocks of 1024 nodes: every
+// block writes its partial and counts itself done; the block that finds itself last (after a
+// fence, so every partial is visible) combines all partials, `per` consecutive ones per thread
+// then lanes and warps, which is again the perfect tree over them. `counter` is zeroed by the
+// launcher before the launch.
+__global__ void __launch_bounds__(kGroup) pairwise_fused(const float* __restrict__ x, long long n, int L, int block,
+                                                         float* partials, unsigned* counter, int per,
+                                                         float* __restrict__ out) {
+  __shared__ float s[kGroup / 32];
+  __shared__ int last;
+  const float r = leaves_block(x, n, L, block, s);
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x] = r;
+    __threadfence();
+    last = atomicAdd(counter, 1u) == gridDim.x - 1 ? 1 : 0;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const float* p = partials + (long long)threadIdx.x * per;
+  float v;
+  switch (per) {
+    case 1: v = chunk_tree<1>(p); break;
+    case 2: v = chunk_tree<2>(p); break;
+    case 4: v = chunk_tree<4>(p); break;
+    case 8: v = chunk_tree<8>(p); break;
+    case 16: v = chunk_tree<16>(p); break;
+    case 32: v = chunk_tree<32>(p); break;
+    default: v = chunk_tree<64>(p); break;
+  }
+  const float t = fast_block_tree(v, s);
+  if (threadIdx.x == 0) out[0] = t;
 }
 
 __global__ void __launch_bounds__(kGroup) pairwise_combine_fast(const float* __restrict__ in, float* __restrict__ out) {
@@ -326,6 +379,18 @@ int tgcb_sum_pairwise_f32(const float* x, uint64_t n, int block, float* out, voi
   const long long nodes = 1ll << L;
   const int uniform = (n % (uint64_t)nodes) == 0 ? 1 : 0;
   float* buf = static_cast<float*>(scratch);
+  // One launch where the leaf level fills 256..16384 blocks of 1024 nodes (the partials and the
+  // counter fit in the scratch the size function promises: 4 * nodes / 256 bytes or more).
+  if (uniform && nodes >= 256ll * kFastSpan && nodes <= 16384ll * kFastSpan) {
+    const long long grid = nodes / kFastSpan;
+    unsigned* counter = reinterpret_cast<unsigned*>(buf + grid);
+    cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(unsigned), s);
+    if (e != cudaSuccess) return report(TGCB_E_CUDA, "pairwise counter reset", e);
+    pairwise_fused<<<(unsigned)grid, kGroup, 0, s>>>(x, (long long)n, L, block, buf, counter, (int)(grid / kGroup), out);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return report(TGCB_E_CUDA, "pairwise_fused", e);
+    return TGCB_OK;
+  }
   // Perfect-tree levels of 1024 values per block where the level is wide enough; the
   // 256-per-block kernels finish narrow levels and irregular (non-uniform) leaves.
   const bool fast0 = uniform && nodes >= kFastSpan;

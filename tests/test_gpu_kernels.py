@@ -91,7 +91,7 @@ def test_summation_vectors_bit_exact_to_tgc(cuda, summ):
 
 
 @pytest.mark.parametrize(
-    "n", [1, 2, 7, 8, 9, 17, 255, 256, 257, 1000, 4096, 12345, 65537, 196608, 1000003, (1 << 21) + 3, 3 << 20, 1 << 22]
+    "n", [1, 2, 7, 8, 9, 17, 255, 256, 257, 1000, 4096, 12345, 65537, 196608, 1000003, (1 << 21) + 3, 3 << 20, 1 << 22, 1 << 24]
 )
 @pytest.mark.parametrize("block", [1, 3, 8, 16])
 def test_pairwise_any_length_any_block(cuda, n, block):
