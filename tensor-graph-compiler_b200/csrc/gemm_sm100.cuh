@@ -303,6 +303,59 @@ __device__ __forceinline__ void gemm_body(const TgcbArgs& args, const TgcbTmaDes
       const int tm = tile / TILES_N;
       const int tn = tile % TILES_N;
       const long long row0 = (long long)tm * BM + quad * 32;
+      if constexpr (Epi::VEC4) {
+        // 8 columns of the warp's 32 rows per step: lane = row coming out of TMEM; after the
+        // transpose lane takes 4 consecutive columns (one 16-byte access) of row 16*it + lane/2.
+        // 16-byte slots are XOR-swizzled by (row/4)%2 so the writes (8 rows per phase) and the
+        // reads (4 rows x 2 slots per phase) each hit all 32 banks once.
+        constexpr int C8 = BN / 4 / 8;
+        const int cbase = part * (BN / 4);
+        uint4* st4 = reinterpret_cast<uint4*>(stage);
+        typename Epi::Loads4 cur[2], nxt[2];
+#pragma unroll
+        for (int it = 0; it < 2; ++it)
+          cur[it] = Epi::load4(args, row0 + 16 * it + (lane >> 1), (long long)tn * BN + cbase + 4 * (lane & 1));
+        bool ok = true;
+        if (lane == 0) ok = bar_wait(tfull_bar(acc), acc_phase, abort_flag, args.status, TGCB_STATUS_TIMEOUT_EPILOGUE);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < C8; ++c) {
+          uint32_t r[8];
+          tmem_ld8(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + cbase + c * 8), r);
+          st4[lane * 2 + (0 ^ ((lane >> 2) & 1))] = make_uint4(r[0], r[1], r[2], r[3]);
+          st4[lane * 2 + (1 ^ ((lane >> 2) & 1))] = make_uint4(r[4], r[5], r[6], r[7]);
+          __syncwarp();
+          const long long col0 = (long long)tn * BN + cbase + c * 8;
+          if (c + 1 < C8) {
+#pragma unroll
+            for (int it = 0; it < 2; ++it) nxt[it] = Epi::load4(args, row0 + 16 * it + (lane >> 1), col0 + 8 + 4 * (lane & 1));
+          }
+#pragma unroll
+          for (int it = 0; it < 2; ++it) {
+            const int rr = 16 * it + (lane >> 1);
+            const int qq = lane & 1;
+            const uint4 v = st4[rr * 2 + (qq ^ ((rr >> 2) & 1))];
+            if constexpr (INT8) {
+              Epi::apply4(args, row0 + rr, col0 + 4 * qq, make_int4((int)v.x, (int)v.y, (int)v.z, (int)v.w), cur[it]);
+            } else {
+              Epi::apply4(args, row0 + rr, col0 + 4 * qq,
+                          make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w)),
+                          cur[it]);
+            }
+          }
+          __syncwarp();
+#pragma unroll
+          for (int it = 0; it < 2; ++it) cur[it] = nxt[it];
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) bar_arrive(tempty_bar(acc));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+        continue;
+      }
       constexpr int CHUNKS = BN / 32;  // 8-column chunks per warp: 64 columns each
       const int chunk0 = part * CHUNKS;
       // Side inputs of the first chunk are fetched before waiting for the accumulator,

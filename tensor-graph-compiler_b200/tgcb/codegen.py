@@ -908,9 +908,11 @@ class Lowering:
             _LOAD_NAME.sub(lambda m: f"L.{m.group(1)}" if m.group(1) in fetched else m.group(1), ln) for ln in comps + st
         )
         epi_name = f"Epi_{kname}"
+        vec4 = self._gemm_vec4_epilogue(name, stores, M, N, acc_t)
         epi = (
             f"struct {epi_name} {{\n"
-            f"  struct Loads {{\n{members}  }};\n"
+            + (vec4 or "  static constexpr bool VEC4 = false;\n")
+            + f"  struct Loads {{\n{members}  }};\n"
             f"  static __device__ __forceinline__ Loads load(const TgcbArgs& args, long long row, long long col) {{\n"
             f"    Loads L;\n"
             f"    if (row < {M}LL && col < {N}LL) {{\n{load_body}    }}\n"
@@ -943,6 +945,86 @@ class Lowering:
             launches=[launch],
             bracketing=how,
             nodes=[name] + list(requests),
+        )
+
+    def _gemm_vec4_epilogue(self, name: str, stores: list[str], M: int, N: int, acc_t: str) -> str | None:
+        """Members of the epilogue struct for four consecutive columns per call (VEC4).
+
+        The tcgen05 kernel hands ``apply4`` one row and columns col..col+3 (col a multiple of
+        4): side inputs that are contiguous along the row arrive as one 16-byte load, column
+        vectors (biases, scales) too, values that do not depend on the column once, and every
+        store is one 16-byte store. The arithmetic is the scalar epilogue's, written out once
+        per column. None when N or a stored type does not allow 16-byte accesses.
+        """
+        vec_t = {"float": "float4", "int": "int4"}
+        if N % 4 or any(ctype(self.values[r].dtype) not in vec_t for r in stores):
+            return None
+        per_col = []
+        for j in range(4):
+            def resolve(n, idx, j=j):
+                return f"acc_{j}" if n == name else None
+
+            eb = ExprBuilder(self.values, self.producers, self._pointer_of, resolve, indent="    ")
+            vals = [eb.value(r, ("row", f"c{j}")) for r in stores]
+            per_col.append((eb, vals))
+
+        def rename(text: str, j: int) -> str:
+            return re.sub(r"\b(ld|e|cat)_(\d+)\b", lambda m: f"{m.group(1)}_{m.group(2)}_{j}", text)
+
+        members, body, sub = [], [], {}
+        infos = [eb.load_info for eb, _ in per_col]
+        for k, (var, t, ptr, off) in enumerate(infos[0]):
+            offs = [infos[j][k][3] for j in range(4)]
+            if all("c" + str(j) not in offs[j] for j in range(4)) and len(set(offs)) == 1:
+                members.append(f"    {t} {var};")
+                body.append(f"      L.{var} = __ldg(reinterpret_cast<const {t}*>({ptr}) + {off});")
+                for j in range(4):
+                    sub[f"{var}_{j}"] = f"L.{var}"
+                continue
+            m = re.fullmatch(r"\(c0(?: \+ \(row\)\*(\d+)LL)?\)", off)
+            if t in vec_t and m and (m.group(1) is None or int(m.group(1)) % 4 == 0) and all(
+                offs[j] == off.replace("c0", f"c{j}") for j in range(4)
+            ):
+                members.append(f"    {vec_t[t]} {var};")
+                body.append(f"      L.{var} = __ldg(reinterpret_cast<const {vec_t[t]}*>(reinterpret_cast<const {t}*>({ptr}) + {off}));")
+                for j, lane in enumerate("xyzw"):
+                    sub[f"{var}_{j}"] = f"L.{var}.{lane}"
+                continue
+            for j in range(4):
+                vj, tj, pj, oj = infos[j][k]
+                members.append(f"    {tj} {vj}_{j};")
+                body.append(f"      L.{vj}_{j} = __ldg(reinterpret_cast<const {tj}*>({pj}) + {oj});")
+                sub[f"{vj}_{j}"] = f"L.{vj}_{j}"
+        comps = []
+        for j, (eb, _) in enumerate(per_col):
+            for line in eb.lines:
+                if _LOAD_LINE.match(line):
+                    continue
+                comps.append(rename(line, j))
+        finals = [[rename(v, j) for v in vals] for j, (_, vals) in enumerate(per_col)]
+        for i, r in enumerate(stores):
+            t = ctype(self.values[r].dtype)
+            parts = ", ".join(f"({t})({finals[j][i]})" for j in range(4))
+            comps.append(
+                f"    *reinterpret_cast<{vec_t[t]}*>(reinterpret_cast<{t}*>({PTR(r)}) + (row * {N}LL + col)) = "
+                f"make_{vec_t[t]}({parts});"
+            )
+        pattern = re.compile(r"\b(?:ld|e|cat)_\d+_\d\b")
+        comp_body = "\n".join(pattern.sub(lambda m: sub.get(m.group(0), m.group(0)), ln) for ln in comps)
+        cols = "    const long long c0 = col, c1 = col + 1, c2 = col + 2, c3 = col + 3;\n"
+        accs = "".join(f"    const {acc_t} acc_{j} = acc.{lane};\n" for j, lane in enumerate("xyzw"))
+        member_text = "\n".join(members) + "\n" if members else "    int unused;\n"
+        return (
+            "  static constexpr bool VEC4 = true;\n"
+            f"  struct Loads4 {{\n{member_text}  }};\n"
+            "  static __device__ __forceinline__ Loads4 load4(const TgcbArgs& args, long long row, long long col) {\n"
+            "    Loads4 L;\n"
+            + cols
+            + f"    if (row < {M}LL && col < {N}LL) {{\n" + "".join(b + "\n" for b in body) + "    }\n"
+            "    return L;\n  }\n"
+            f"  static __device__ __forceinline__ void apply4(const TgcbArgs& args, long long row, long long col, "
+            f"const {vec_t[acc_t]} acc, const Loads4& L) {{\n"
+            f"    if (row >= {M}LL || col >= {N}LL) return;\n" + cols + accs + comp_body + "\n  }\n"
         )
 
     def _gemm_simt_kernel(self, kname, epi_name, M, N, K, is_int, a_base, a_flip, b_base, b_flip) -> str:

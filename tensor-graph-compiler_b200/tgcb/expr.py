@@ -201,6 +201,8 @@ class ExprBuilder:
         self.counter = 0
         self.indent = indent
         self.loads: set[str] = set()
+        # (variable, C type, base pointer expression, element offset expression) per load
+        self.load_info: list[tuple[str, str, str, str]] = []
 
     def fresh(self, stem: str) -> str:
         self.counter += 1
@@ -233,6 +235,7 @@ class ExprBuilder:
             var = self.fresh("ld")
             off = linearise(idx, self.sizes(name))
             self.emit(f"const {t} {var} = __ldg(reinterpret_cast<const {t}*>({ptr}) + {off});")
+            self.load_info.append((var, t, ptr, off))
             return var
         node = self.producers.get(name)
         if node is None:
