@@ -150,6 +150,15 @@ int tgcb_sum_pairwise_f32(const float* x, uint64_t n, int block, float* out, voi
  * the whole vector's _pairwise value bit for bit. Writes *out (device). */
 int tgcb_sum_perfect_tree_f32(const float* partials, uint32_t count, float* out, void* stream);
 
+/* One head of attention in one pass over the keys, float32, replacing
+ * tgc/analysis/attention.py:97-137 (streaming_attention): out = softmax(q k^T / sqrt(width)) v
+ * with the running maximum and sum rescaled per block of keys, the score matrix never stored.
+ * q [sq, width], k and v [sk, width], out [sq, width], all row-major float32 device arrays,
+ * 16-byte aligned; width 16, 32, 64 or 128. Agrees with tgc's float32 result up to summation
+ * order (the kernel's key block is 64). */
+int tgcb_streaming_attention_f32(const float* q, const float* k, const float* v, uint32_t sq, uint32_t sk,
+                                 uint32_t width, float* out, void* stream);
+
 /* Sequential sum from 0.0f left to right, bit-exact to tgc/analysis/summation.py:56-61. */
 int tgcb_sum_sequential_f32(const float* x, uint64_t n, float* out, void* stream);
 

@@ -100,6 +100,11 @@ SIGNATURES = {
     ),
     "tgcb_sum_sequential_f32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]),
     "tgcb_sum_perfect_tree_f32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p]),
+    "tgcb_streaming_attention_f32": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+         ctypes.c_void_p, ctypes.c_void_p],
+    ),
     "tgcb_sum_pairwise_f32_noalloc": (
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p],
