@@ -42,6 +42,13 @@ struct TgcbArgs {
 #define INFINITY __int_as_float(0x7f800000)
 #endif
 
+// Approximate functions for TF32 GEMM epilogues only, whose results are compared at TF32
+// tolerance; every other kernel calls CUDA's accurate functions. tanh(u) = 1 - 2 / (1 + e^(2u))
+// and sigmoid(u) = 1 / (1 + e^(-u)) from the hardware exponential and a correctly rounded
+// reciprocal: absolute error ~1e-6 or less over the whole range, +-1 and 0/1 at the ends.
+__device__ __forceinline__ float tgcb_tanh_approx(float u) { return 1.0f - 2.0f * __frcp_rn(1.0f + __expf(2.0f * u)); }
+__device__ __forceinline__ float tgcb_sigmoid_approx(float u) { return __frcp_rn(1.0f + __expf(-u)); }
+
 __device__ __forceinline__ long long tgcb_min_ll(long long a, long long b) { return a < b ? a : b; }
 __device__ __forceinline__ long long tgcb_max_ll(long long a, long long b) { return a > b ? a : b; }
 

@@ -40,7 +40,7 @@ from dataclasses import dataclass, field
 
 from tgcb import ir
 from tgcb.errors import CodegenError
-from tgcb.expr import ExprBuilder, _broadcast_index, ctype, delinearise
+from tgcb.expr import ExprBuilder, _broadcast_index, contract_fma, ctype, delinearise
 
 NUM_SMS = 148
 _LOAD_LINE = re.compile(r"^\s*const (.+?) (ld_\d+) = (.*);$")
@@ -884,7 +884,9 @@ class Lowering:
                 return "acc"
             return None
 
-        eb = ExprBuilder(self.values, self.producers, self._pointer_of, resolve, indent="    ")
+        # A TF32 GEMM's epilogue is compared at TF32 tolerance, so it may use the approximate
+        # exp/tanh/sigmoid and fused multiply-adds; the int8 epilogue stays exact.
+        eb = ExprBuilder(self.values, self.producers, self._pointer_of, resolve, indent="    ", approx=not is_int)
         st = []
         for r in stores:
             v = eb.value(r, ("row", "col"))
@@ -901,6 +903,8 @@ class Lowering:
                 loads.append(m.groups())
             else:
                 comps.append(line)
+        if not is_int:
+            comps = contract_fma(comps, st)
         members = "".join(f"    {t} {n};\n" for t, n, _ in loads) or "    int unused;\n"
         load_body = "".join(f"      L.{n} = {e};\n" for t, n, e in loads)
         fetched = {n for _, n, _ in loads}
@@ -964,7 +968,7 @@ class Lowering:
             def resolve(n, idx, j=j):
                 return f"acc_{j}" if n == name else None
 
-            eb = ExprBuilder(self.values, self.producers, self._pointer_of, resolve, indent="    ")
+            eb = ExprBuilder(self.values, self.producers, self._pointer_of, resolve, indent="    ", approx=acc_t == "float")
             vals = [eb.value(r, ("row", f"c{j}")) for r in stores]
             per_col.append((eb, vals))
 
@@ -996,11 +1000,11 @@ class Lowering:
                 body.append(f"      L.{vj}_{j} = __ldg(reinterpret_cast<const {tj}*>({pj}) + {oj});")
                 sub[f"{vj}_{j}"] = f"L.{vj}_{j}"
         comps = []
-        for j, (eb, _) in enumerate(per_col):
-            for line in eb.lines:
-                if _LOAD_LINE.match(line):
-                    continue
-                comps.append(rename(line, j))
+        for j, (eb, vals) in enumerate(per_col):
+            lines = [ln for ln in eb.lines if not _LOAD_LINE.match(ln)]
+            if acc_t == "float":
+                lines = contract_fma(lines, vals)
+            comps.extend(rename(ln, j) for ln in lines)
         finals = [[rename(v, j) for v in vals] for j, (_, vals) in enumerate(per_col)]
         for i, r in enumerate(stores):
             t = ctype(self.values[r].dtype)

@@ -24,6 +24,8 @@ propagate NaN like torch does.
 
 from __future__ import annotations
 
+import re
+
 import struct
 from collections.abc import Callable, Sequence
 
@@ -78,10 +80,12 @@ def _wrap(op: str, a: str, b: str, d) -> str:
     return f"(({ctype(d)})(({u}){a} {op} ({u}){b}))"
 
 
-def unary_c(name: str, a: str, src, out) -> str:
+def unary_c(name: str, a: str, src, out, approx: bool = False) -> str:
     t = ctype(out)
     if _is_int(src) and out.is_float:
         a = f"(({t}){a})"
+    if approx and t == "float" and name in ("exp", "tanh", "sigmoid"):
+        return {"exp": f"__expf({a})", "tanh": f"tgcb_tanh_approx({a})", "sigmoid": f"tgcb_sigmoid_approx({a})"}[name]
     if name == "neg":
         return f"(-{a})" if not _is_int(out) else _wrap("-", "0", a, out)
     if name == "exp":
@@ -191,7 +195,9 @@ class ExprBuilder:
         pointer_of: Callable[[str], str | None],
         resolve: Callable[[str, tuple[str, ...]], str | None] | None = None,
         indent: str = "    ",
+        approx: bool = False,
     ):
+        self.approx = approx  # hardware-approximate exp/tanh/sigmoid (TF32 GEMM epilogues only)
         self.values = graph_values
         self.producers = producers
         self.pointer_of = pointer_of
@@ -254,7 +260,7 @@ class ExprBuilder:
             if op == "cast":
                 expr = cast_c(args[0], srcs[0], v.dtype)
             elif len(args) == 1:
-                expr = unary_c(op, args[0], srcs[0], v.dtype)
+                expr = unary_c(op, args[0], srcs[0], v.dtype, self.approx)
             else:
                 a, b = args
                 if _is_int(v.dtype) is False and any(_is_int(s) for s in srcs):
@@ -306,3 +312,61 @@ class ExprBuilder:
         raise CodegenError(
             f"{name} ({op}) has to be materialised by its own kernel before another kernel reads it"
         )
+
+
+_MUL_PREFIX = "(((float)"
+
+
+def _split_binary(expr: str) -> tuple[str, str, str] | None:
+    """(a, op, b) of a float binary_c expression ``(((float)a) op ((float)b))``, else None."""
+    if not (expr.startswith(_MUL_PREFIX) and expr.endswith("))")):
+        return None
+    inner = expr[len(_MUL_PREFIX):-2]
+    for op in ("*", "+", "-"):
+        sep = f") {op} ((float)"
+        if inner.count(sep) == 1:
+            a, b = inner.split(sep)
+            return a, op, b
+    return None
+
+
+_DEF = re.compile(r"^(\s*)const float (e_\d+) = (.*);$")
+
+
+def contract_fma(lines: list[str], finals: Sequence[str]) -> list[str]:
+    """Fuse a float product used once, by an add or subtract, into one fmaf (single rounding).
+
+    For TF32 GEMM epilogues only, whose results are compared at TF32 tolerance; everywhere else
+    each operation rounds on its own, as the reference's per-operation execution does.
+    """
+    uses: dict[str, int] = {}
+    for text in list(lines) + list(finals):
+        for name in re.findall(r"\be_\d+\b", text):
+            uses[name] = uses.get(name, 0) + 1
+    products: dict[str, tuple[str, str]] = {}
+    for line in lines:
+        m = _DEF.match(line)
+        if m:
+            parts = _split_binary(m.group(3))
+            if parts and parts[1] == "*":
+                products[m.group(2)] = (parts[0], parts[2])
+    fused: set[str] = set()
+    out = []
+    for line in lines:
+        m = _DEF.match(line)
+        parts = _split_binary(m.group(3)) if m else None
+        if parts and parts[1] in "+-":
+            a, op, b = parts
+            # uses[] counts the definition too: a product read once appears twice
+            if a in products and uses.get(a) == 2 and a not in fused:
+                pa, pb = products[a]
+                c = f"((float){b})" if op == "+" else f"(-((float){b}))"
+                fused.add(a)
+                line = f"{m.group(1)}const float {m.group(2)} = __fmaf_rn((float){pa}, (float){pb}, {c});"
+            elif b in products and uses.get(b) == 2 and b not in fused:
+                pa, pb = products[b]
+                pa = pa if op == "+" else f"(-((float){pa}))"
+                fused.add(b)
+                line = f"{m.group(1)}const float {m.group(2)} = __fmaf_rn((float){pa}, (float){pb}, ((float){a}));"
+        out.append(line)
+    return [ln for ln in out if not ((m := _DEF.match(ln)) and m.group(2) in fused)]

@@ -35,7 +35,7 @@ def test_mlp_is_layernorm_then_two_gemms():
     assert [s.kind for s in mod.steps] == ["row", "gemm", "gemm"]
     ln, g1, g2 = mod.steps
     assert len(ln.writes) == 1  # the normalised x, read by the first GEMM
-    assert "tanhf" in g1.source  # GELU fused into the first GEMM's epilogue
+    assert "tgcb_tanh_approx" in g1.source  # GELU fused into the first GEMM's epilogue
     assert "tgcb_gemm::gemm_body<8192, 4096, 1024, false, false, true" in g1.source
     assert "tgcb_gemm::gemm_body<8192, 1024, 4096, false, false, true" in g2.source
 
@@ -128,3 +128,29 @@ def test_odd_gemm_rows_use_the_simt_fallback():
 def test_compile_error_is_a_codegen_error():
     with pytest.raises(CodegenError):
         runtime.compile_source('extern "C" __global__ void k() { this is not cuda; }')
+
+
+def test_fma_contraction_only_fuses_single_use_products():
+    from tgcb.expr import contract_fma
+
+    lines = [
+        "    const float e_1 = (((float)a) * ((float)b));",
+        "    const float e_2 = (((float)e_1) + ((float)c));",
+        "    const float e_3 = (((float)a) * ((float)c));",
+        "    const float e_4 = (((float)d) - ((float)e_3));",
+        "    const float e_5 = (((float)a) * ((float)d));",
+        "    const float e_6 = (((float)e_5) + ((float)e_5));",
+    ]
+    out = contract_fma(lines, ["e_2", "e_4", "e_6"])
+    assert out[0] == "    const float e_2 = __fmaf_rn((float)a, (float)b, ((float)c));"
+    assert out[1] == "    const float e_4 = __fmaf_rn((float)(-((float)a)), (float)c, ((float)d));"
+    assert out[2:] == lines[4:]  # e_5 is read twice: left alone
+
+
+def test_tf32_epilogues_approximate_int8_epilogues_exact():
+    mlp = runtime.generate(workloads.mlp_graph(ir.Builder, rows=1024))[3]
+    assert "tgcb_tanh_approx" in mlp.steps[1].source and "tanhf" not in mlp.steps[1].source
+    int8 = runtime.generate(workloads.int8_linear_graph(ir.Builder, ir.INT8, ir.INT32, ir.FLOAT32, rows=256))[3]
+    assert "__fmaf_rn" not in int8.steps[0].source and "approx" not in int8.steps[0].source
+    cone = runtime.generate(workloads.cone_graph(ir.Builder))[3]
+    assert "expf(" in cone.steps[0].source and "__expf" not in cone.steps[0].source
