@@ -12,8 +12,8 @@
 //   Where a level is uniform and at least 1024 wide, a block takes 1024 consecutive nodes
 //   instead (4 per thread in registers, xor shuffles across lanes, 8 warp partials last):
 //   the same perfect tree with one barrier per block instead of eight. When that level has
-//   256..16384 blocks the whole sum is one launch: the last block to finish combines every
-//   block's partial (pairwise_fused).
+//   256..16384 blocks, one more block combines all block partials (pairwise_final, a
+//   programmatic dependent launch that is resident before the leaves finish).
 // Every addition is the one _pairwise performs, so the result is bit-identical.
 //
 // Sequential sum (summation.py:56-61) is one dependent chain of n float additions; one
@@ -200,25 +200,22 @@ __device__ __forceinline__ float chunk_tree(const float* p) {
   return v[0];
 }
 
-// Whole sum in one launch when the leaf level has 256 to 16384 blocks of 1024 nodes: every
-// block writes its partial and counts itself done; the block that finds itself last (after a
-// fence, so every partial is visible) combines all partials, `per` consecutive ones per thread
-// then lanes and warps, which is again the perfect tree over them. `counter` is zeroed by the
-// launcher before the launch.
-__global__ void __launch_bounds__(kGroup) pairwise_fused(const float* __restrict__ x, long long n, int L, int block,
-                                                         float* partials, unsigned* counter, int per,
-                                                         float* __restrict__ out) {
+// The two launches of a wide uniform sum. The leaf kernel lets its dependent launch start at
+// once (programmatic dependent launch), so the final kernel is resident and waiting when the
+// last leaf block retires, instead of paying a launch gap. The final kernel (one block) waits
+// for the leaf grid's writes, then takes `per` consecutive block partials per thread, adds them
+// as a perfect tree, then lanes and warps as before: again the perfect tree over all partials.
+__global__ void __launch_bounds__(kGroup) pairwise_leaves_pdl(const float* __restrict__ x, long long n, int L,
+                                                              int block, float* __restrict__ out) {
+  asm volatile("griddepcontrol.launch_dependents;");
   __shared__ float s[kGroup / 32];
-  __shared__ int last;
   const float r = leaves_block(x, n, L, block, s);
-  if (threadIdx.x == 0) {
-    partials[blockIdx.x] = r;
-    __threadfence();
-    last = atomicAdd(counter, 1u) == gridDim.x - 1 ? 1 : 0;
-  }
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
+  if (threadIdx.x == 0) out[blockIdx.x] = r;
+}
+
+__global__ void __launch_bounds__(kGroup) pairwise_final(const float* partials, int per, float* __restrict__ out) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ float s[kGroup / 32];
   const float* p = partials + (long long)threadIdx.x * per;
   float v;
   switch (per) {
@@ -379,16 +376,24 @@ int tgcb_sum_pairwise_f32(const float* x, uint64_t n, int block, float* out, voi
   const long long nodes = 1ll << L;
   const int uniform = (n % (uint64_t)nodes) == 0 ? 1 : 0;
   float* buf = static_cast<float*>(scratch);
-  // One launch where the leaf level fills 256..16384 blocks of 1024 nodes (the partials and the
-  // counter fit in the scratch the size function promises: 4 * nodes / 256 bytes or more).
+  // Two launches where the leaf level fills 256..16384 blocks of 1024 nodes: the leaf partials,
+  // then one block that combines them, launched as a programmatic dependent of the first.
   if (uniform && nodes >= 256ll * kFastSpan && nodes <= 16384ll * kFastSpan) {
     const long long grid = nodes / kFastSpan;
-    unsigned* counter = reinterpret_cast<unsigned*>(buf + grid);
-    cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(unsigned), s);
-    if (e != cudaSuccess) return report(TGCB_E_CUDA, "pairwise counter reset", e);
-    pairwise_fused<<<(unsigned)grid, kGroup, 0, s>>>(x, (long long)n, L, block, buf, counter, (int)(grid / kGroup), out);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return report(TGCB_E_CUDA, "pairwise_fused", e);
+    pairwise_leaves_pdl<<<(unsigned)grid, kGroup, 0, s>>>(x, (long long)n, L, block, buf);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return report(TGCB_E_CUDA, "pairwise_leaves_pdl", e);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kGroup);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, pairwise_final, (const float*)buf, (int)(grid / kGroup), out);
+    if (e != cudaSuccess) return report(TGCB_E_CUDA, "pairwise_final", e);
     return TGCB_OK;
   }
   // Perfect-tree levels of 1024 values per block where the level is wide enough; the

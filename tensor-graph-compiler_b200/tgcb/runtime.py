@@ -352,7 +352,8 @@ class CompiledGraph:
             raise ConfigError(f"no value supplied for {missing}")
         with torch.cuda.device(self.device):
             s = stream if stream is not None else torch.cuda.current_stream(self.device)
-            ptrs = self.input_pointers(arena, feeds)
+            with torch.cuda.stream(s):  # input copies are ordered before the kernels that read them
+                ptrs = self.input_pointers(arena, feeds)
             arr = (ctypes.c_void_p * max(1, len(ptrs)))(*ptrs)
             rc = _lib.load().tgcb_plan_run(self._plan, ctypes.c_void_p(arena.data_ptr()), arr, len(ptrs), ctypes.c_void_p(s.cuda_stream))
             _lib.check(rc, "running the compiled graph")
@@ -384,7 +385,8 @@ class CompiledGraph:
         torch = self._torch
         with torch.cuda.device(self.device):
             s = stream if stream is not None else torch.cuda.current_stream(self.device)
-            ptrs = self.input_pointers(arena, feeds)
+            with torch.cuda.stream(s):
+                ptrs = self.input_pointers(arena, feeds)
             arr = (ctypes.c_void_p * max(1, len(ptrs)))(*ptrs)
             n = len(self.module.launches)
             ms = (ctypes.c_float * max(1, n))()
