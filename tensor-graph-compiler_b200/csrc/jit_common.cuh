@@ -44,10 +44,16 @@ struct TgcbArgs {
 
 // Approximate functions for TF32 GEMM epilogues only, whose results are compared at TF32
 // tolerance; every other kernel calls CUDA's accurate functions. tanh(u) = 1 - 2 / (1 + e^(2u))
-// and sigmoid(u) = 1 / (1 + e^(-u)) from the hardware exponential and a correctly rounded
-// reciprocal: absolute error ~1e-6 or less over the whole range, +-1 and 0/1 at the ends.
-__device__ __forceinline__ float tgcb_tanh_approx(float u) { return 1.0f - 2.0f * __frcp_rn(1.0f + __expf(2.0f * u)); }
-__device__ __forceinline__ float tgcb_sigmoid_approx(float u) { return __frcp_rn(1.0f + __expf(-u)); }
+// and sigmoid(u) = 1 / (1 + e^(-u)) from the hardware exponential and the hardware reciprocal
+// (PTX rcp.approx, about 1 ulp; its argument 1 + e^x is never below 1, and 1/inf is 0):
+// absolute error ~1e-6 or less over the whole range, +-1 and 0/1 at the ends.
+__device__ __forceinline__ float tgcb_rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float tgcb_tanh_approx(float u) { return 1.0f - 2.0f * tgcb_rcp_approx(1.0f + __expf(2.0f * u)); }
+__device__ __forceinline__ float tgcb_sigmoid_approx(float u) { return tgcb_rcp_approx(1.0f + __expf(-u)); }
 
 __device__ __forceinline__ long long tgcb_min_ll(long long a, long long b) { return a < b ? a : b; }
 __device__ __forceinline__ long long tgcb_max_ll(long long a, long long b) { return a > b ? a : b; }

@@ -912,17 +912,19 @@ class Lowering:
             _LOAD_NAME.sub(lambda m: f"L.{m.group(1)}" if m.group(1) in fetched else m.group(1), ln) for ln in comps + st
         )
         epi_name = f"Epi_{kname}"
-        vec4 = self._gemm_vec4_epilogue(name, stores, M, N, acc_t)
+        # every 128 x 256 tile lies inside the output: the epilogue needs no bounds checks
+        whole_tiles = M % 128 == 0 and N % 256 == 0
+        vec4 = self._gemm_vec4_epilogue(name, stores, M, N, acc_t, whole_tiles)
         epi = (
             f"struct {epi_name} {{\n"
             + (vec4 or "  static constexpr bool VEC4 = false;\n")
             + f"  struct Loads {{\n{members}  }};\n"
             f"  static __device__ __forceinline__ Loads load(const TgcbArgs& args, long long row, long long col) {{\n"
             f"    Loads L;\n"
-            f"    if (row < {M}LL && col < {N}LL) {{\n{load_body}    }}\n"
-            f"    return L;\n  }}\n"
+            + (f"    {{\n{load_body}    }}\n" if whole_tiles else f"    if (row < {M}LL && col < {N}LL) {{\n{load_body}    }}\n")
+            + f"    return L;\n  }}\n"
             f"  static __device__ __forceinline__ void apply(const TgcbArgs& args, long long row, long long col, const {acc_t} acc, const Loads& L) {{\n"
-            f"    if (row >= {M}LL || col >= {N}LL) return;\n" + comp_body + "\n  }\n};\n"
+            + ("" if whole_tiles else f"    if (row >= {M}LL || col >= {N}LL) return;\n") + comp_body + "\n  }\n};\n"
         )
         reads = {a_base, b_base}  # plus whatever the epilogue loads (recorded by _pointer_of)
         tma_ok = all((op.cols * op.elem_bytes) % 16 == 0 for op in (opa, opb))
@@ -951,7 +953,8 @@ class Lowering:
             nodes=[name] + list(requests),
         )
 
-    def _gemm_vec4_epilogue(self, name: str, stores: list[str], M: int, N: int, acc_t: str) -> str | None:
+    def _gemm_vec4_epilogue(self, name: str, stores: list[str], M: int, N: int, acc_t: str,
+                            whole_tiles: bool = False) -> str | None:
         """Members of the epilogue struct for four consecutive columns per call (VEC4).
 
         The tcgen05 kernel hands ``apply4`` one row and columns col..col+3 (col a multiple of
@@ -1024,11 +1027,11 @@ class Lowering:
             "  static __device__ __forceinline__ Loads4 load4(const TgcbArgs& args, long long row, long long col) {\n"
             "    Loads4 L;\n"
             + cols
-            + f"    if (row < {M}LL && col < {N}LL) {{\n" + "".join(b + "\n" for b in body) + "    }\n"
+            + ("    {\n" if whole_tiles else f"    if (row < {M}LL && col < {N}LL) {{\n") + "".join(b + "\n" for b in body) + "    }\n"
             "    return L;\n  }\n"
             f"  static __device__ __forceinline__ void apply4(const TgcbArgs& args, long long row, long long col, "
             f"const {vec_t[acc_t]} acc, const Loads4& L) {{\n"
-            f"    if (row >= {M}LL || col >= {N}LL) return;\n" + cols + accs + comp_body + "\n  }\n"
+            + ("" if whole_tiles else f"    if (row >= {M}LL || col >= {N}LL) return;\n") + cols + accs + comp_body + "\n  }\n"
         )
 
     def _gemm_simt_kernel(self, kname, epi_name, M, N, K, is_int, a_base, a_flip, b_base, b_flip) -> str:
