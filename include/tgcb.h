@@ -66,7 +66,7 @@ typedef struct tgcb_launch_desc {
   uint32_t grid[3];
   uint32_t block[3];
   uint32_t smem_bytes;
-  uint32_t is_gemm;
+  uint32_t is_gemm;      /* 0: plain kernel; 1: GEMM; 2: GEMM launched as clusters of two CTAs */
   tgcb_operand_desc a;
   tgcb_operand_desc b;
 } tgcb_launch_desc;

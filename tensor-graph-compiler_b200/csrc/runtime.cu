@@ -301,7 +301,25 @@ int launch_one(DeviceState* st, LaunchState& ls, TgcbArgs& args, void* arena, co
       }
     }
     void* params[3] = {&args, &ls.ta, &ls.tb};
-    e = cudaLaunchKernel(reinterpret_cast<const void*>(ls.kernel), grid, block, params, d.smem_bytes, s);
+    if (d.is_gemm == 2) {
+      // two-SM GEMM: clusters of two CTAs (an even grid)
+      if ((d.grid[0] & 1u) != 0u) return fail(TGCB_E_INVALID, "%s: a pair GEMM needs an even grid", d.kernel);
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = grid;
+      cfg.blockDim = block;
+      cfg.dynamicSmemBytes = d.smem_bytes;
+      cfg.stream = s;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      e = cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(ls.kernel), params);
+    } else {
+      e = cudaLaunchKernel(reinterpret_cast<const void*>(ls.kernel), grid, block, params, d.smem_bytes, s);
+    }
   } else {
     void* params[1] = {&args};
     e = cudaLaunchKernel(reinterpret_cast<const void*>(ls.kernel), grid, block, params, d.smem_bytes, s);

@@ -43,6 +43,7 @@ from tgcb.errors import CodegenError
 from tgcb.expr import ExprBuilder, _broadcast_index, contract_fma, ctype, delinearise
 
 NUM_SMS = 148
+PAIR_GEMM = True  # whole 256 x 256 tiles run on SM pairs
 _LOAD_LINE = re.compile(r"^\s*const (.+?) (ld_\d+) = (.*);$")
 _LOAD_NAME = re.compile(r"\b(ld_\d+)\b")
 GEMM_THREADS = 576  # tgcb_gemm::THREADS: TMA warp, MMA warp, 16 epilogue warps
@@ -68,6 +69,7 @@ class Launch:
     block: tuple[int, int, int]
     smem: int = 0
     gemm: tuple[GemmOperand, GemmOperand] | None = None
+    pair: bool = False  # two-SM GEMM: launched as clusters of two CTAs
 
 
 @dataclass
@@ -929,15 +931,24 @@ class Lowering:
         reads = {a_base, b_base}  # plus whatever the epilogue loads (recorded by _pointer_of)
         tma_ok = all((op.cols * op.elem_bytes) % 16 == 0 for op in (opa, opb))
         if tma_ok:
+            # Whole 256 x 256 tiles with the four-column epilogue run on SM pairs (two CTAs of a
+            # cluster share one tcgen05.mma.cta_group::2 tile); everything else on single SMs.
+            pair = vec4 is not None and M % 256 == 0 and N % 256 == 0 and PAIR_GEMM
+            body = "gemm_body_pair" if pair else "gemm_body"
             kernel = (
                 f'extern "C" __global__ void __launch_bounds__({GEMM_THREADS}, 1) {kname}(const TgcbArgs args, '
                 "const __grid_constant__ TgcbTmaDesc ta, const __grid_constant__ TgcbTmaDesc tb) {\n"
-                f"  tgcb_gemm::gemm_body<{M}, {N}, {K}, {'true' if is_int else 'false'}, "
+                f"  tgcb_gemm::{body}<{M}, {N}, {K}, {'true' if is_int else 'false'}, "
                 f"{'true' if opa.mn_major else 'false'}, {'true' if opb.mn_major else 'false'}, {epi_name}>(args, &ta, &tb);\n}}\n"
             )
-            tiles = ((M + 127) // 128) * ((N + 255) // 256)
-            launch = Launch(kname, (max(1, min(tiles, NUM_SMS)), 1, 1), (GEMM_THREADS, 1, 1), smem=-1, gemm=(opa, opb))
+            if pair:
+                grid = 2 * max(1, min((M // 256) * (N // 256), NUM_SMS // 2))
+            else:
+                grid = max(1, min(((M + 127) // 128) * ((N + 255) // 256), NUM_SMS))
+            launch = Launch(kname, (grid, 1, 1), (GEMM_THREADS, 1, 1), smem=-1, gemm=(opa, opb), pair=pair)
             how = "tcgen05." + ("kind::i8, int32 accumulator in TMEM (exact)" if is_int else "kind::tf32, fp32 accumulator in TMEM, K in steps of 8")
+            if pair:
+                how += "; SM pairs (cta_group::2), 256 x 256 tiles"
         else:
             kernel = self._gemm_simt_kernel(kname, epi_name, M, N, K, is_int, a_base, a_flip, b_base, b_flip)
             launch = Launch(kname, ((M * ((N + 15) // 16) + 127) // 128, 1, 1), (128, 1, 1))

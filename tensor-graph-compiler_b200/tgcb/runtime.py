@@ -35,7 +35,7 @@ from tgcb.errors import CodegenError, ConfigError, DeviceError
 from tgcb.passes import default_pipeline
 
 CSRC = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "csrc")
-HEADERS = ("jit_common.cuh", "gemm_sm100.cuh")
+HEADERS = ("jit_common.cuh", "gemm_sm100.cuh", "gemm_sm100_pair.cuh")
 SUPPORTED_OPS = {
     "add", "sub", "mul", "div", "maximum", "minimum", "neg", "exp", "log", "sqrt", "tanh", "relu",
     "sigmoid", "reciprocal", "abs", "step", "cast", "matmul", "sum", "mean", "max", "reshape",
@@ -44,6 +44,7 @@ SUPPORTED_OPS = {
 # tgcb_gemm::SMEM_BYTES: 4 stages of (128 + 256) rows x 128 B, barriers, the epilogue
 # transpose tiles (16 warps x 32 x 8 words) and 1 KB of alignment slack.
 GEMM_SMEM = 4 * (128 + 256) * 128 + 256 + 16 * 32 * 8 * 4 + 1024
+GEMM_PAIR_SMEM = 6 * (128 + 128) * 128 + 256 + 16 * 32 * 8 * 4 + 1024  # tgcb_gemm::P_SMEM_BYTES
 _PLACEHOLDER = re.compile(r"@P<([^>]+)>@")
 
 TORCH_DTYPES = {}
@@ -166,6 +167,8 @@ def _render(lowering: Lowering, steps: list[Step], offsets: dict[str, int]) -> s
     parts = ['#include "jit_common.cuh"']
     if any(s.kind == "gemm" for s in steps):
         parts.append('#include "gemm_sm100.cuh"')
+    if any(ln.pair for s in steps for ln in s.launches):
+        parts.append('#include "gemm_sm100_pair.cuh"')
     for s in steps:
         parts.append(f"// step {s.kind}: {s.label}" + (f"\n// bracketing: {s.bracketing}" if s.bracketing else ""))
         parts.append(_PLACEHOLDER.sub(sub, s.source))
@@ -226,10 +229,12 @@ def generate(graph, *, pipeline=None, optimise: bool = True) -> tuple:
             d.grid = (ctypes.c_uint32 * 3)(*ln.grid)
             d.block = (ctypes.c_uint32 * 3)(*ln.block)
             if ln.gemm is not None:
-                d.is_gemm = 1
-                d.smem_bytes = GEMM_SMEM
+                # 1: one-SM kernel; 2: two-SM kernel, launched as clusters of two CTAs, each of
+                # which stages 128 columns of B
+                d.is_gemm = 2 if ln.pair else 1
+                d.smem_bytes = GEMM_PAIR_SMEM if ln.pair else GEMM_SMEM
                 d.a = _operand_desc(ln.gemm[0], lowering, offsets, 128)
-                d.b = _operand_desc(ln.gemm[1], lowering, offsets, 256)
+                d.b = _operand_desc(ln.gemm[1], lowering, offsets, 128 if ln.pair else 256)
             else:
                 d.is_gemm = 0
                 d.smem_bytes = max(0, ln.smem)

@@ -36,15 +36,17 @@ def test_mlp_is_layernorm_then_two_gemms():
     ln, g1, g2 = mod.steps
     assert len(ln.writes) == 1  # the normalised x, read by the first GEMM
     assert "tgcb_tanh_approx" in g1.source  # GELU fused into the first GEMM's epilogue
-    assert "tgcb_gemm::gemm_body<8192, 4096, 1024, false, false, true" in g1.source
-    assert "tgcb_gemm::gemm_body<8192, 1024, 4096, false, false, true" in g2.source
+    # whole 256 x 256 tiles: both GEMMs run on SM pairs
+    assert "tgcb_gemm::gemm_body_pair<8192, 4096, 1024, false, false, true" in g1.source
+    assert "tgcb_gemm::gemm_body_pair<8192, 1024, 4096, false, false, true" in g2.source
+    assert all(ln.pair and ln.grid[0] % 2 == 0 for ln in g1.launches + g2.launches)
 
 
 def test_int8_linear_is_one_int8_gemm_with_fused_dequant():
     mod = runtime.generate(workloads.int8_linear_graph(ir.Builder, ir.INT8, ir.INT32, ir.FLOAT32))[3]
     assert [s.kind for s in mod.steps] == ["gemm"]
     # int8 operands read directly, both K-major (the weight arrives transposed)
-    assert "gemm_body<8192, 4096, 4096, true, false, false" in mod.steps[0].source
+    assert "gemm_body_pair<8192, 4096, 4096, true, false, false" in mod.steps[0].source
     assert len(mod.steps[0].writes) == 2  # the int32 accumulator and the dequantised output
 
 

@@ -163,6 +163,39 @@ def test_gemm_layouts(cuda, ta, tb, kind):
         assert torch.equal(out, ref)
 
 
+@pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("kind", ["f32", "i8"])
+def test_pair_gemm_layouts(cuda, ta, tb, kind):
+    """Whole 256 x 256 tiles run on SM pairs (tcgen05 cta_group::2): every operand major, ragged K."""
+    M, N, K = 512, 768, 96 if kind == "f32" else 320
+    b = ir.Builder()
+    ash, bsh = ([K, M] if ta else [M, K]), ([N, K] if tb else [K, N])
+    dt = ir.FLOAT32 if kind == "f32" else ir.INT8
+    a = b.input(ash, dt, name="a")
+    w = b.input(bsh, dt, name="b")
+    av, wv = (a, w) if kind == "f32" else (b.cast(a, ir.INT32), b.cast(w, ir.INT32))
+    if ta:
+        av = b.transpose(av, [1, 0])
+    if tb:
+        wv = b.transpose(wv, [1, 0])
+    g = b.finish(b.relu(b.matmul(av, wv)) if kind == "f32" else b.matmul(av, wv))
+    from tgcb import runtime
+
+    assert all(ln.pair for s in runtime.generate(g)[3].steps if s.kind == "gemm" for ln in s.launches)
+    gen = torch.Generator().manual_seed(5)
+    if kind == "f32":
+        feeds = {"a": torch.randn(ash, generator=gen), "b": torch.randn(bsh, generator=gen)}
+    else:
+        feeds = {"a": torch.randint(-128, 128, ash, generator=gen, dtype=torch.int8),
+                 "b": torch.randint(-128, 128, bsh, generator=gen, dtype=torch.int8)}
+    _, (out,) = run(g, feeds)
+    ref = interp.run(g, feeds)[0]
+    if kind == "f32":
+        assert rel_err(out, ref) < TF32_TOL
+    else:
+        assert torch.equal(out, ref)
+
+
 def test_simt_fallback_gemm(cuda):
     b = ir.Builder()
     a = b.input([5, 3], name="a")
