@@ -62,6 +62,8 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--train-rows", type=int, default=65536, help="global batch of the train workload (profiling uses a small one)")
+    p.add_argument("--train-buckets", choices=["final", "per_gradient"], default="final",
+                   help="train: one grouped gradient all-reduce after the backward, or one per gradient as it becomes final")
     return p.parse_args()
 
 
@@ -557,6 +559,7 @@ class TrainWorkload:
     unit = "train steps/s"
     dtype = "tf32"
     scaling = "strong"
+    buckets = "final"
     global_rows = 65536
     payload = 2 * 1024 * 4096 * 4 + 4096 * 4 + 1024 * 4
 
@@ -582,7 +585,8 @@ class TrainWorkload:
         from tgcb import parallel, workloads
 
         self.world = world
-        self.step_obj = parallel.DataParallelTrainStep(self.global_rows, world, self.rank, dist=dist, device=device)
+        self.step_obj = parallel.DataParallelTrainStep(self.global_rows, world, self.rank, dist=dist, device=device,
+                                                       buckets=self.buckets)
         self.g = self.step_obj.graph
         feeds = workloads.mlp_inputs(rows=self.global_rows, target=True)
         x, t = self.step_obj.shard(feeds["x"], feeds["target"])
@@ -736,6 +740,7 @@ def _main(json_out) -> int:
     wl = WORKLOADS[args.workload](rank)
     if args.workload == "train":
         wl.global_rows = args.train_rows
+        wl.buckets = args.train_buckets
         wl.setup(device, dist, n)
     elif args.workload == "longsum":
         wl.setup(device, dist, n)
@@ -858,7 +863,8 @@ def _main(json_out) -> int:
             "dtype": wl.dtype,
             "data": "synthetic: seeded torch.randn inputs and random-init weights of the workload's shapes",
             "config": {**wl.config(), "parallelism": wl.parallelism(n) if hasattr(wl, "parallelism") else f"dp{n}: " + (
-                f"{wl.global_rows // n} rows per GPU, gradients averaged by NCCL all-reduce overlapped with the backward"
+                f"{wl.global_rows // n} rows per GPU, gradients averaged by NCCL all-reduce "
+                + ("as one grouped call after the backward" if args.train_buckets == "final" else "per gradient, overlapped with the backward")
                 if args.workload == "train" else "independent row shards per GPU, no collective")},
             "roofline": {
                 "bound": dk["bound"],

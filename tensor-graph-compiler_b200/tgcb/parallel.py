@@ -66,7 +66,14 @@ class DataParallelTrainStep:
     """
 
     def __init__(self, global_rows: int, world: int, rank: int, *, d: int = 1024, f: int = 4096, dist=None,
-                 device=None, executor: Callable | None = None):
+                 device=None, executor: Callable | None = None, buckets: str = "final"):
+        """``buckets``: "per_gradient" starts each gradient's all-reduce as soon as the launch that
+        finalises it is queued; "final" averages all gradients in one grouped NCCL call after the
+        last launch (one collective's latency instead of four; the GEMMs occupy every SM, so
+        collectives queued beside them barely overlap anyway)."""
+        if buckets not in ("per_gradient", "final"):
+            raise ConfigError(f"unknown bucketing {buckets!r}")
+        self.buckets = buckets
         self.global_rows = global_rows
         self.world = world
         self.rank = rank
@@ -98,8 +105,14 @@ class DataParallelTrainStep:
         if self.dist is None or self.world == 1:
             return
         if self.dist.get_backend() == "nccl":
-            for t in tensors:
-                self.dist.all_reduce(t, op=self.dist.ReduceOp.AVG)
+            if len(tensors) > 1:
+                from torch.distributed.distributed_c10d import _coalescing_manager
+
+                with _coalescing_manager(device=tensors[0].device):
+                    for t in tensors:
+                        self.dist.all_reduce(t, op=self.dist.ReduceOp.AVG)
+            else:
+                self.dist.all_reduce(tensors[0], op=self.dist.ReduceOp.AVG)
         else:
             for t in tensors:
                 self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
@@ -130,17 +143,20 @@ class DataParallelTrainStep:
                 e.record(main)
                 timing.append((s, e))
 
-        for k in self.finals:
-            run(done, k + 1 - done)
-            done = k + 1
-            if self.dist is not None and self.world > 1:
-                ev = torch.cuda.Event()
-                ev.record(main)
-                with torch.cuda.stream(self.comm):
-                    self.comm.wait_event(ev)
-                    self._average([outs[i] for i in self.out_at[k]])
+        if self.buckets == "per_gradient":
+            for k in self.finals:
+                run(done, k + 1 - done)
+                done = k + 1
+                if self.dist is not None and self.world > 1:
+                    ev = torch.cuda.Event()
+                    ev.record(main)
+                    with torch.cuda.stream(self.comm):
+                        self.comm.wait_event(ev)
+                        self._average([outs[i] for i in self.out_at[k]])
         if done < total:
             run(done, total - done)
+        if self.buckets == "final" and self.dist is not None and self.world > 1:
+            self._average(list(outs))
         if self.dist is not None and self.world > 1:
             main.wait_stream(self.comm)
         return outs
