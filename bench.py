@@ -409,8 +409,15 @@ class ConeWorkload(GraphWorkload):
 
 
 class Int8Workload(GraphWorkload):
+    """The int8 linear layer as a serving step: the float32 activations are quantised per token
+    on the GPU (tgcb.quantize, bit-exact to tgc's per_row_schemes + quantise), then the
+    compiled graph runs the int8 GEMM with int32 accumulation and the fused dequantisation.
+    The weight is quantised per output channel once, outside the step (tgc hoists it the same
+    way: passes/hoisting.py)."""
+
     name = "int8"
     dtype = "int8 x int8 -> int32, f32 dequant"
+    rows, k, n = 8192, 4096, 4096
 
     def graph(self):
         from tgcb import ir, workloads
@@ -418,26 +425,132 @@ class Int8Workload(GraphWorkload):
         return workloads.int8_linear_graph(ir.Builder, ir.INT8, ir.INT32, ir.FLOAT32)
 
     def feeds(self):
+        """Host-side inputs for the CPU restatement: float32 activations, quantised weight."""
         import torch
 
         from oracle import quantize as oq
         from tgcb import workloads
 
         ins = workloads.int8_inputs(seed=self.rank)
-        qa, sa = oq.quantise_rows(ins["a"].numpy())
         qwt, sw = oq.quantise_rows(ins["w"].T.contiguous().numpy())
-        return {"qa": torch.from_numpy(qa), "qwt": torch.from_numpy(qwt),
-                "sa": torch.from_numpy(sa).reshape(-1, 1), "sw": torch.from_numpy(sw).reshape(1, -1)}
+        return {"a": ins["a"], "qwt": torch.from_numpy(qwt), "sw": torch.from_numpy(sw).reshape(1, -1)}
 
     def config(self):
-        return {"workload": "int8 linear: qa [8192,4096] x qwt^T [4096,4096] -> int32 acc -> *sa *sw (f32)",
-                "int_ops_per_exec": 2 * 8192 * 4096 * 4096, "l2": L2_NOTE}
+        return {"workload": "int8 linear: A [8192,4096] f32 quantised per token on the GPU -> qa x qwt^T [4096,4096] "
+                            "-> int32 acc -> *sa *sw (f32); W quantised once outside the step",
+                "int_ops_per_exec": 2 * self.rows * self.k * self.n, "l2": L2_NOTE}
+
+    def setup(self, device) -> None:
+        import torch
+
+        from tgcb import quantize, workloads
+        from tgcb.runtime import compile_graph
+
+        self.g = self.graph()
+        self.compiled = compile_graph(self.g, device=device.index)
+        ins = workloads.int8_inputs(seed=self.rank)
+        self.a_host = ins["a"].pin_memory()
+        self.a_dev = ins["a"].to(device)
+        qwt, sw = quantize.quantise_rows(ins["w"].T.contiguous().to(device))
+        self.weights = {"qwt": qwt, "sw": sw.reshape(1, -1)}
+        self.sets = []
+        for _ in range(2):  # two independent buffer sets for the pipelined end-to-end run
+            qa = torch.empty(self.rows, self.k, dtype=torch.int8, device=device)
+            sa = torch.empty(self.rows, dtype=torch.float32, device=device)
+            self.sets.append({"a": torch.empty_like(self.a_dev), "qa": qa, "sa": sa, "arena": self.compiled.new_arena(),
+                              "feeds": {"qa": qa, "sa": sa.reshape(-1, 1), **self.weights}})
+        self.arena = self.sets[0]["arena"]
+        quantize.quantise_rows_into(self.a_dev, self.sets[0]["qa"], self.sets[0]["sa"])
+        outs = self.compiled.function(self.arena, self.sets[0]["feeds"])
+        self.out_host = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+        self.out_host2 = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+        torch.cuda.synchronize()
+        self.compiled.check_status()
+
+    @property
+    def cpu_feeds(self):
+        if not hasattr(self, "_cpu_feeds"):
+            self._cpu_feeds = self.feeds()
+        return self._cpu_feeds
+
+    @cpu_feeds.setter
+    def cpu_feeds(self, value):
+        self._cpu_feeds = value
+
+    def launches_per_step(self) -> int:
+        return 1 + self.compiled.launches_per_call
+
+    def step_profiled(self) -> list[float]:
+        import torch
+
+        from tgcb import quantize
+
+        st = self.sets[0]
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        quantize.quantise_rows_into(self.a_dev, st["qa"], st["sa"])
+        e.record()
+        ms = self.compiled.run_profiled(st["arena"], st["feeds"])[1]
+        return [s.elapsed_time(e)] + ms
+
+    def _e2e_call(self, st, out_host, stream) -> None:
+        from tgcb import quantize
+
+        st["a"].copy_(self.a_host, non_blocking=True)
+        quantize.quantise_rows_into(st["a"], st["qa"], st["sa"], stream=stream)
+        outs = self.compiled.function(st["arena"], st["feeds"], stream=stream)
+        for o, h in zip(outs, out_host, strict=True):
+            h.copy_(o, non_blocking=True)
+
+    def step_e2e(self) -> None:
+        import torch
+
+        self._e2e_call(self.sets[0], self.out_host, torch.cuda.current_stream())
+
+    def run_e2e(self, steps: int) -> float:
+        """As GraphWorkload.run_e2e: float32 activations in from pinned host memory, quantised,
+        multiplied and dequantised, both outputs back to pinned host memory, alternating two
+        streams and two buffer sets."""
+        import torch
+
+        if not hasattr(self, "streams"):
+            self.streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+        cur = torch.cuda.current_stream()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(cur)
+        for st in self.streams:
+            st.wait_event(start)
+        for i in range(steps):
+            st = self.streams[i % 2]
+            with torch.cuda.stream(st):
+                self._e2e_call(self.sets[i % 2], self.out_host if i % 2 == 0 else self.out_host2, st)
+        for st in self.streams:
+            cur.wait_stream(st)
+        end.record(cur)
+        end.synchronize()
+        return start.elapsed_time(end)
+
+    def h2d_bytes(self) -> int:
+        return self.a_host.numel() * 4
+
+    def kernel_work(self) -> list[dict]:
+        quant = self.rows * self.k * 4 + self.rows * self.k + self.rows * 4
+        return [{"name": "quantise_rows_i8", "kind": "quantise", "bound": "hbm", "work": quant}] + GraphWorkload.kernel_work(self)
 
     def cpu_program(self):
         from oracle import interp
+        from oracle import quantize as oq
 
         g = self.g
-        return lambda feeds: interp.run(g, feeds)
+
+        def run(feeds):
+            qa, sa = oq.quantise_rows(feeds["a"].numpy())
+            import torch
+
+            return interp.run(g, {"qa": torch.from_numpy(qa), "sa": torch.from_numpy(sa).reshape(-1, 1),
+                                  "qwt": feeds["qwt"], "sw": feeds["sw"]})
+
+        return run
 
 
 class LongSumWorkload:

@@ -338,6 +338,48 @@ __global__ void __launch_bounds__(256) quantise_rows(const float* __restrict__ x
   }
 }
 
+// Rows whose length is a multiple of 1024 (and 16-byte aligned): one CTA per row, each thread
+// holding V float4 of its row in registers (columns 4(t + 256k) .. +3). max|x| is exact in any
+// order and the quantisation is elementwise, so this layout changes no result; it only makes
+// every load 16 bytes and every store 4 bytes wide.
+template <int V>
+__global__ void __launch_bounds__(256) quantise_rows_vec(const float* __restrict__ x, long long cols, int8_t* __restrict__ q,
+                                                         float* __restrict__ scale) {
+  __shared__ float red[8];
+  const long long r = blockIdx.x;
+  const float4* row = reinterpret_cast<const float4*>(x + r * cols);
+  float4 v[V];
+  float m = 0.0f;
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    v[k] = __ldg(row + threadIdx.x + 256 * k);
+    const float a[4] = {fabsf(v[k].x), fabsf(v[k].y), fabsf(v[k].z), fabsf(v[k].w)};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m = (a[i] > m || a[i] != a[i]) ? a[i] : m;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float other = __shfl_xor_sync(0xffffffffu, m, o);
+    m = (other > m || other != other) ? other : m;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float mm = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) mm = (red[w] > mm || red[w] != red[w]) ? red[w] : mm;
+  const float s = (mm == 0.0f) ? 1.0f : (float)((double)mm / 127.0);
+  if (threadIdx.x == 0) scale[r] = s;
+  char4* qrow = reinterpret_cast<char4*>(q + r * cols);
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const float e[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+    signed char b[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) b[i] = (signed char)(int)fminf(fmaxf(rintf(__fdiv_rn(e[i], s)), -128.0f), 127.0f);
+    qrow[threadIdx.x + 256 * k] = make_char4(b[0], b[1], b[2], b[3]);
+  }
+}
+
 int levels_for(uint64_t n, int block) {
   // deepest L with floor(n / 2^(L-1)) > block, i.e. every node above depth L is internal
   int L = 0;
@@ -451,6 +493,18 @@ int tgcb_quantise_rows_i8(const float* x, int64_t rows, int64_t cols, int8_t* q,
     return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_quantise_rows_i8", "null pointer");
   if (rows < 1 || cols < 1) return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_quantise_rows_i8", "there is nothing to quantise");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(q)) & 15u) == 0;
+  const long long per = cols / 1024;  // float4 per thread in quantise_rows_vec
+  if (aligned && cols % 1024 == 0 && rows <= 0x7fffffffll && (per == 1 || per == 2 || per == 4 || per == 8 || per == 16)) {
+    if (per == 1) quantise_rows_vec<1><<<(unsigned)rows, 256, 0, s>>>(x, cols, q, scale);
+    if (per == 2) quantise_rows_vec<2><<<(unsigned)rows, 256, 0, s>>>(x, cols, q, scale);
+    if (per == 4) quantise_rows_vec<4><<<(unsigned)rows, 256, 0, s>>>(x, cols, q, scale);
+    if (per == 8) quantise_rows_vec<8><<<(unsigned)rows, 256, 0, s>>>(x, cols, q, scale);
+    if (per == 16) quantise_rows_vec<16><<<(unsigned)rows, 256, 0, s>>>(x, cols, q, scale);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return report(TGCB_E_CUDA, "quantise_rows_vec", e);
+    return TGCB_OK;
+  }
   const unsigned grid = (unsigned)(rows < 148 * 8 ? rows : 148 * 8);
   if (cols <= 256 * 4)
     quantise_rows<4><<<grid, 256, 0, s>>>(x, rows, cols, q, scale);

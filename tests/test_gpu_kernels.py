@@ -140,7 +140,7 @@ def test_quantiser_bit_exact_to_tgc(cuda):
         assert np.array_equal(s.cpu().numpy(), gold[f"{name}/scale"].astype(np.float32))
 
 
-@pytest.mark.parametrize("rows,cols", [(3, 1), (17, 1000), (64, 4096), (5, 5000)])
+@pytest.mark.parametrize("rows,cols", [(3, 1), (17, 1000), (64, 4096), (5, 5000), (8, 1024), (4, 2048), (3, 3072), (2, 8192), (2, 16384)])
 def test_quantiser_shapes(cuda, rows, cols):
     x = torch.randn(rows, cols, generator=torch.Generator().manual_seed(cols)) * 3
     q, s = quantize.quantise_rows(x.cuda())
