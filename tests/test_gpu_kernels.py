@@ -149,6 +149,23 @@ def test_quantiser_shapes(cuda, rows, cols):
     assert np.array_equal(s.cpu().numpy(), so)
 
 
+@pytest.mark.parametrize("m", [127.0, 12.7, 3.0, 1e-3])
+def test_quantiser_ties(cuda, m):
+    """Values whose quotient by the row scale sits on or next to a half-integer: the fast
+    reciprocal path must hand those to the exact quotient (round half to even)."""
+    s = np.float32(m / 127.0)
+    k = np.arange(-127, 127, dtype=np.float32)
+    on = (k + np.float32(0.5)) * s
+    near = np.concatenate([on, np.nextafter(on, np.float32(np.inf)), np.nextafter(on, np.float32(-np.inf))])
+    row = np.concatenate([[np.float32(m)], near, np.zeros(1024 - 1 - near.size % 1024, dtype=np.float32)])
+    row = row[: (row.size // 1024) * 1024].astype(np.float32)
+    x = np.tile(row, (3, 1))
+    q, sc = quantize.quantise_rows(torch.from_numpy(x).cuda())
+    qo, so = oq.quantise_rows(x)
+    assert np.array_equal(q.cpu().numpy(), qo)
+    assert np.array_equal(sc.cpu().numpy(), so)
+
+
 def test_quantiser_input_checks(cuda):
     with pytest.raises(ConfigError):
         quantize.quantise_rows(torch.ones(4, device="cuda"))
