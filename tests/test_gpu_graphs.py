@@ -254,6 +254,25 @@ def test_column_full_and_generic_reductions(cuda):
     assert np.array_equal(out[0].numpy(), bracketing.col_parts(feeds["x"].numpy(), rows_per_part))
 
 
+def test_integer_reductions_exact(cuda):
+    """int8 sums widen to int32 (accumulator_for, tgc/ir/dtype.py:139-151); int32 row, column and
+    full sums and maxima are exact, so they must equal the interpreter's bit for bit. (tgc's
+    interpreter hands back torch's int64 for integer sums; values are compared in the graph's
+    declared int32, with inputs small enough that no int32 sum wraps.)"""
+    b = ir.Builder()
+    q = b.input([64, 300], ir.INT8, name="q")
+    n = b.input([257, 33], ir.INT32, name="n")
+    g = b.finish(b.sum(q, [1]), b.sum(q, [0]), b.sum(n, [0]), b.max(n, [1]), b.sum(n, [0, 1]))
+    gen = torch.Generator().manual_seed(11)
+    feeds = {"q": torch.randint(-128, 128, (64, 300), generator=gen, dtype=torch.int8),
+             "n": torch.randint(-(1 << 16), 1 << 16, (257, 33), generator=gen, dtype=torch.int32)}
+    _, out = run(g, feeds)
+    ref = interp.run(g, feeds)
+    for o, r in zip(out, ref, strict=True):
+        assert o.dtype == torch.int32 and o.shape == r.shape
+        assert torch.equal(o, r.to(torch.int32))
+
+
 def test_views_and_broadcasts(cuda):
     b = ir.Builder()
     x = b.input([6, 8], name="x")
