@@ -1,0 +1,76 @@
+"""tgc's executor tests (tests/test_executor.py: TestExecution) re-pointed at the B200 backend:
+every graph of its GRAPHS table and the transpose pair/chain of passes/layout.py, printed by
+tgc (tests/golden/graphs/exec_*.tgc), compiled with and without the pass pipeline, checked
+against the oracle on the same seeded feeds, then run again on one arena with seeds 1-7
+(a kernel that reads a buffer before writing it passes the first call and fails later).
+Tolerance: rtol = atol = 1e-5 for float32 graphs, 5e-3 of the largest output for graphs with
+a TF32 GEMM (tgc holds its own compiled path bit-identical to its interpreter because both are
+torch on the CPU; here the arithmetic is the GPU's)."""
+
+from __future__ import annotations
+
+import os
+
+import pytest
+import torch
+from conftest import GOLDEN
+
+from oracle import interp
+from tgcb import serialize
+from tgcb.errors import ConfigError
+from tgcb.runtime import compile_graph
+
+pytestmark = pytest.mark.gpu
+
+NAMES = ["chain", "softmax", "layernorm", "mlp", "diamond", "branching", "transposed_pair", "transposed_chain"]
+
+
+def load(name):
+    with open(os.path.join(GOLDEN, "graphs", f"exec_{name}.tgc")) as f:
+        return serialize.loads(f.read())
+
+
+def agree(got, want, gemm: bool) -> bool:
+    for a, b in zip(got, want, strict=True):
+        a = a.detach().cpu()
+        if a.shape != b.shape:
+            return False
+        if gemm:
+            if float((a.double() - b.double()).abs().max()) > 5e-3 * float(b.double().abs().max()):
+                return False
+        elif not torch.allclose(a.float(), b.float(), rtol=1e-5, atol=1e-5):
+            return False
+    return True
+
+
+@pytest.mark.parametrize("optimise", [True, False], ids=["pipeline", "no_pipeline"])
+@pytest.mark.parametrize("name", NAMES)
+def test_every_executor_graph_matches(cuda, name, optimise):
+    g = load(name)
+    gemm = any(n.op.name == "matmul" for n in g.nodes)
+    compiled = compile_graph(g, optimise=optimise)
+    feeds = interp.random_feeds(g, seed=0, positive=True)
+    out = compiled({k: v.cuda() for k, v in feeds.items()})
+    torch.cuda.synchronize()
+    compiled.check_status()
+    assert agree(out, interp.run(g, feeds), gemm), name
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_the_arena_survives_reuse(cuda, name):
+    g = load(name)
+    gemm = any(n.op.name == "matmul" for n in g.nodes)
+    compiled = compile_graph(g)
+    arena = compiled.new_arena()
+    for seed in range(1, 8):
+        feeds = interp.random_feeds(g, seed=seed, positive=True)
+        out = [o.clone() for o in compiled.function(arena, {k: v.cuda() for k, v in feeds.items()})]
+        torch.cuda.synchronize()
+        assert agree(out, interp.run(g, feeds), gemm), (name, seed)
+    compiled.check_status()
+
+
+def test_a_missing_input_is_reported(cuda):
+    compiled = compile_graph(load("softmax"))
+    with pytest.raises(ConfigError, match="no value supplied"):
+        compiled({})
