@@ -110,3 +110,28 @@ def test_two_nccl_ranks_sum_the_long_vector_bit_exact(tmp_path):
         want = json.load(f)["longsum"]["pairwise"]
     for r in range(world):
         assert float(torch.load(os.path.join(tmp_path, f"sum{r}.pt"))[0]) == want
+
+
+def test_gradients_match_torch_autograd(cuda):
+    """The reverse-mode graph's gradients on the GPU against torch.autograd of the same MLP loss
+    in float64 on the CPU (independent of tgc's rules and of the oracle; TF32 tolerance)."""
+    import math
+
+    rows = 512
+    feeds = workloads.mlp_inputs(rows=rows, target=True)
+    step = parallel.DataParallelTrainStep(rows, 1, 0)
+    grads = step.step({k: v.cuda() for k, v in feeds.items()})
+    torch.cuda.synchronize()
+    step.compiled.check_status()
+    p = {k: feeds[k].double().requires_grad_(k in parallel.GRADS) for k in feeds}
+    x = p["x"]
+    cen = x - x.mean(1, keepdim=True)
+    ln = cen / torch.sqrt((cen * cen).mean(1, keepdim=True) + workloads.LN_EPS)
+    h = ln @ p["w1"] + p["b1"]
+    g = 0.5 * h * (1 + torch.tanh(math.sqrt(2 / math.pi) * (h + 0.044715 * h ** 3)))
+    y = g @ p["w2"] + p["b2"]
+    loss = ((y - p["target"]) ** 2).mean()
+    ref = torch.autograd.grad(loss, [p[k] for k in parallel.GRADS])
+    for got, want in zip(grads, ref, strict=True):
+        assert got.shape == want.shape
+        assert rel_err(got, want) < TF32_TOL
