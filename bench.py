@@ -341,12 +341,16 @@ class GraphWorkload:
         out = []
         for s in self.compiled.module.steps:
             if s.kind == "gemm":
-                node = low.producers[s.label]
-                M, K = low.sizes(node.inputs[0])
-                N = low.sizes(node.inputs[1])[1]
-                is_int = node.output.dtype.name == "int32"
+                # one GEMM, or a chain of two in one launch (label "first+second")
+                work = 0
+                for label in s.label.split("+"):
+                    node = low.producers[label]
+                    M, K = low.sizes(node.inputs[0])
+                    N = low.sizes(node.inputs[1])[1]
+                    is_int = node.output.dtype.name == "int32"
+                    work += 2 * M * N * K
                 for ln in s.launches:
-                    out.append({"name": ln.kernel, "kind": s.kind, "bound": "tensor", "work": 2 * M * N * K,
+                    out.append({"name": ln.kernel, "kind": s.kind, "bound": "tensor", "work": work,
                                 "type": "int8" if is_int else "tf32"})
                 continue
             rbytes = sum(low.values[r].bytes for r in s.reads if r in low.values)

@@ -60,15 +60,24 @@ typedef struct tgcb_operand_desc {
 } tgcb_operand_desc;
 
 /* One kernel launch of a plan. Plain kernels take TgcbArgs; GEMM kernels take TgcbArgs
- * and two tensor maps that tgcb_plan_run encodes from a and b. */
+ * and two tensor maps that tgcb_plan_run encodes from a and b; a chain (is_gemm 3: two GEMMs
+ * in one launch of clusters of two CTAs, the second reading the first one's output rows) takes
+ * four, from a, b, a2 and b2, and tgcb_plan_run zeroes its counter_bytes of arena at
+ * counter_offset (per-row-block counters) before every launch. Every pair of a chain must be
+ * resident at once: the first launch checks the device's cluster occupancy and fails with
+ * TGCB_E_INVALID when it cannot hold them. */
 typedef struct tgcb_launch_desc {
   char kernel[96];
   uint32_t grid[3];
   uint32_t block[3];
   uint32_t smem_bytes;
-  uint32_t is_gemm;      /* 0: plain kernel; 1: GEMM; 2: GEMM launched as clusters of two CTAs */
+  uint32_t is_gemm;      /* 0: plain kernel; 1: GEMM; 2: GEMM launched as clusters of two CTAs; 3: chain */
   tgcb_operand_desc a;
   tgcb_operand_desc b;
+  tgcb_operand_desc a2;  /* is_gemm 3 only */
+  tgcb_operand_desc b2;  /* is_gemm 3 only */
+  uint64_t counter_offset; /* is_gemm 3 only: bytes from the arena base, 4-byte aligned */
+  uint64_t counter_bytes;
 } tgcb_launch_desc;
 
 /* Library version string. */

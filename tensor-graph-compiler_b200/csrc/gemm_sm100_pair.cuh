@@ -11,6 +11,11 @@
 // empty and accumulator-full barriers of both CTAs (one commit per CTA, no multicast); both
 // CTAs' epilogue warps arrive on the leader's accumulator-empty barrier. Every mbarrier wait is
 // bounded as in the one-SM kernel. No TMA load uses cluster multicast.
+//
+// A chain runs two GEMMs in one persistent launch when the second reads the first one's output
+// rows as its A operand (an MLP block's two linears): the pairs work through a per-pair list of
+// tiles of both GEMMs, and a tile of the second waits only for the row block of the first that
+// it reads, so neither GEMM's last partial wave leaves SMs idle.
 #pragma once
 #include "gemm_sm100.cuh"
 
@@ -71,62 +76,292 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar) : "memory");
 }
 
-template <int M, int N, int K, bool INT8, bool A_MN, bool B_MN, class Epi>
-__device__ __forceinline__ void gemm_body_pair(const TgcbArgs& args, const TgcbTmaDesc* ta, const TgcbTmaDesc* tb) {
+// One GEMM run by the pair kernel: C[M,N] = A[M,K] @ B[K,N] and its generated epilogue.
+template <int M_, int N_, int K_, bool A_MN_, bool B_MN_, class Epi_>
+struct PairGemm {
+  static constexpr int M = M_;
+  static constexpr int N = N_;
+  static constexpr int K = K_;
+  static constexpr bool A_MN = A_MN_;
+  static constexpr bool B_MN = B_MN_;
+  using Epi = Epi_;
   static_assert(Epi::VEC4, "the two-SM kernel uses the four-column epilogue");
   static_assert(M % (2 * BM) == 0 && N % BN == 0, "the two-SM kernel covers whole 256 x 256 tiles");
+  static constexpr int TILES_M = M / (2 * BM);
+  static constexpr int TILES_N = N / BN;
+  static constexpr int NUM_TILES = TILES_M * TILES_N;
+};
+
+// Stands for "no second GEMM" in pair_body.
+struct NoGemm {
+  static constexpr int NUM_TILES = 0;
+  static constexpr int TILES_N = 1;
+};
+
+// The tiles of one GEMM dealt round-robin over the pairs (tile = pair + i * pairs).
+template <int NUM_TILES>
+struct RoundRobin {
+  static __device__ __forceinline__ int count(int pair, int pairs) {
+    return pair < NUM_TILES ? (NUM_TILES - 1 - pair) / pairs + 1 : 0;
+  }
+  static __device__ __forceinline__ int item(int pair, int pairs, int i) { return pair + i * pairs; }
+};
+
+// What every role of one CTA needs: shared-memory stages, barriers, tensor memory, its rank.
+struct PairCta {
+  uint32_t sA, sB, bar0, tmem, rank;
+  volatile int* abort_flag;
+  __device__ __forceinline__ uint32_t full_bar(int s) const { return bar0 + 8u * s; }
+  __device__ __forceinline__ uint32_t empty_bar(int s) const { return bar0 + 8u * (P_STAGES + s); }
+  __device__ __forceinline__ uint32_t tfull_bar(int a) const { return bar0 + 8u * (2 * P_STAGES + a); }
+  __device__ __forceinline__ uint32_t tempty_bar(int a) const { return bar0 + 8u * (2 * P_STAGES + 2 + a); }
+  // chains only (index 2 * P_STAGES + 4 holds the tensor-memory address and the abort flag):
+  // the epilogue warps have stored a first-GEMM tile / the signal warp has published it
+  __device__ __forceinline__ uint32_t stored_bar(int s) const { return bar0 + 8u * (2 * P_STAGES + 5 + s); }
+  __device__ __forceinline__ uint32_t published_bar(int s) const { return bar0 + 8u * (2 * P_STAGES + 7 + s); }
+};
+
+// Position in the ring of operand stages (stage, parity) and of the two accumulators.
+struct StageRing {
+  int stage = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next() {
+    if (++stage == P_STAGES) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
+struct AccRing {
+  int acc = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next() {
+    acc ^= 1;
+    if (acc == 0) phase ^= 1u;
+  }
+};
+
+// Producer (one thread per CTA): this CTA's 128 rows of A and 128 columns of B for every
+// k-block of one tile, completing on the leader's full barrier.
+template <bool INT8, class G>
+__device__ __forceinline__ bool produce_tile(const PairCta& c, const TgcbArgs& args, const TgcbTmaDesc* ta,
+                                             const TgcbTmaDesc* tb, int tile, StageRing& r) {
+  constexpr int EB = INT8 ? 1 : 4;
+  constexpr int KB = ROW_BYTES / EB;
+  constexpr int NUM_KB = (G::K + KB - 1) / KB;
+  constexpr uint32_t PAIR_TX = 2 * (P_A_STAGE + P_B_STAGE);  // both CTAs' halves land on the leader's barrier
+  const int tm = tile / G::TILES_N;
+  const int tn = tile % G::TILES_N;
+  const int arow = tm * 2 * BM + (int)c.rank * BM;      // this CTA's rows of A
+  const int bcol = tn * BN + (int)c.rank * (BN / 2);    // this CTA's columns of B
+  for (int kb = 0; kb < NUM_KB; ++kb) {
+    if (!bar_wait(c.empty_bar(r.stage), r.phase ^ 1u, c.abort_flag, args.status, TGCB_STATUS_TIMEOUT_PRODUCER)) return false;
+    const uint32_t lead_full = cluster_addr(c.full_bar(r.stage), 0);
+    if (c.rank == 0) bar_arrive_expect(c.full_bar(r.stage), PAIR_TX);
+    const uint32_t a_dst = c.sA + r.stage * P_A_STAGE;
+    const uint32_t b_dst = c.sB + r.stage * P_B_STAGE;
+    if (!G::A_MN) {
+      tma_load_2d_pair(a_dst, ta, kb * KB, arow, lead_full);
+    } else {
+#pragma unroll
+      for (int q = 0; q < BM * EB / ROW_BYTES; ++q)
+        tma_load_2d_pair(a_dst + q * (KB * ROW_BYTES), ta, arow + q * (ROW_BYTES / EB), kb * KB, lead_full);
+    }
+    if (!G::B_MN) {
+      tma_load_2d_pair(b_dst, tb, kb * KB, bcol, lead_full);
+    } else {
+#pragma unroll
+      for (int q = 0; q < (BN / 2) * EB / ROW_BYTES; ++q)
+        tma_load_2d_pair(b_dst + q * (KB * ROW_BYTES), tb, bcol + q * (ROW_BYTES / EB), kb * KB, lead_full);
+    }
+    r.next();
+  }
+  return true;
+}
+
+// MMA issue (one thread of the leader): one 256 x 256 tile into accumulator a.acc, then
+// commits that make both CTAs' accumulator-full barriers complete when the tile is done.
+template <bool INT8, class G>
+__device__ __forceinline__ bool mma_tile(const PairCta& c, const TgcbArgs& args, StageRing& r, AccRing& a) {
   constexpr int EB = INT8 ? 1 : 4;
   constexpr int KB = ROW_BYTES / EB;
   constexpr int MMA_K = 32 / EB;
   constexpr int KSTEPS = KB / MMA_K;
-  constexpr int NUM_KB = (K + KB - 1) / KB;
-  constexpr int TILES_M = M / (2 * BM);
-  constexpr int TILES_N = N / BN;
-  constexpr int NUM_TILES = TILES_M * TILES_N;
-  constexpr uint32_t PAIR_TX = 2 * (P_A_STAGE + P_B_STAGE);  // both CTAs' halves land on the leader's barrier
+  constexpr int NUM_KB = (G::K + KB - 1) / KB;
   constexpr uint32_t MN_LAYOUT = INT8 ? 2u : 1u;
   constexpr uint32_t MN_SBO = INT8 ? 1024u : 512u;
   // Instruction descriptor as in the one-SM kernel, with M = 256 (the pair's rows).
   constexpr uint32_t IDESC = (INT8 ? (2u << 4) : (1u << 4)) | (INT8 ? (1u << 7) : (2u << 7)) |
-                             (INT8 ? (1u << 10) : (2u << 10)) | ((A_MN ? 1u : 0u) << 15) | ((B_MN ? 1u : 0u) << 16) |
-                             ((uint32_t)(BN >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
+                             (INT8 ? (1u << 10) : (2u << 10)) | ((G::A_MN ? 1u : 0u) << 15) |
+                             ((G::B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
+  if (!bar_wait(c.tempty_bar(a.acc), a.phase ^ 1u, c.abort_flag, args.status, TGCB_STATUS_TIMEOUT_MMA)) return false;
+  tc_fence_after();
+  const uint32_t d = c.tmem + (uint32_t)(a.acc * BN);
+  for (int kb = 0; kb < NUM_KB; ++kb) {
+    if (!bar_wait(c.full_bar(r.stage), r.phase, c.abort_flag, args.status, TGCB_STATUS_TIMEOUT_MMA)) return false;
+    tc_fence_after();
+    const uint32_t a_base = c.sA + r.stage * P_A_STAGE;
+    const uint32_t b_base = c.sB + r.stage * P_B_STAGE;
+#pragma unroll
+    for (int k = 0; k < KSTEPS; ++k) {
+      const unsigned long long adesc = G::A_MN ? umma_desc(a_base + k * MMA_K * ROW_BYTES, KB * ROW_BYTES, MN_SBO, MN_LAYOUT)
+                                               : umma_desc(a_base + k * 32, 16, 1024);
+      const unsigned long long bdesc = G::B_MN ? umma_desc(b_base + k * MMA_K * ROW_BYTES, KB * ROW_BYTES, MN_SBO, MN_LAYOUT)
+                                               : umma_desc(b_base + k * 32, 16, 1024);
+      mma_pair<INT8>(d, adesc, bdesc, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+    }
+    mma_commit_pair(cluster_addr(c.empty_bar(r.stage), 0));
+    mma_commit_pair(cluster_addr(c.empty_bar(r.stage), 1));
+    r.next();
+  }
+  mma_commit_pair(cluster_addr(c.tfull_bar(a.acc), 0));
+  mma_commit_pair(cluster_addr(c.tfull_bar(a.acc), 1));
+  a.next();
+  return true;
+}
+
+// Epilogue (one warp): its 32 rows x 64 columns of this CTA's half of a tile, 8 columns at a
+// time out of tensor memory, transposed through shared memory so that two lanes hand one
+// row's four consecutive columns to the generated apply4; then the accumulator goes back to
+// the leader.
+template <bool INT8, class G>
+__device__ __forceinline__ bool epilogue_tile(const PairCta& c, const TgcbArgs& args, int tile, AccRing& a, uint4* st4,
+                                              int quad, int cbase, int lane, uint32_t lead_tempty0, uint32_t lead_tempty1) {
+  using Epi = typename G::Epi;
+  constexpr int C8 = BN / 4 / 8;
+  const int tm = tile / G::TILES_N;
+  const int tn = tile % G::TILES_N;
+  const long long row0 = (long long)tm * 2 * BM + (long long)c.rank * BM + quad * 32;
+  typename Epi::Loads4 cur[2], nxt[2];
+#pragma unroll
+  for (int it = 0; it < 2; ++it)
+    cur[it] = Epi::load4(args, row0 + 16 * it + (lane >> 1), (long long)tn * BN + cbase + 4 * (lane & 1));
+  bool ok = true;
+  if (lane == 0) ok = bar_wait(c.tfull_bar(a.acc), a.phase, c.abort_flag, args.status, TGCB_STATUS_TIMEOUT_EPILOGUE);
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  if (!ok) return false;
+  tc_fence_after();
+#pragma unroll 1
+  for (int q = 0; q < C8; ++q) {
+    uint32_t v8[8];
+    tmem_ld8(c.tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(a.acc * BN + cbase + q * 8), v8);
+    st4[lane * 2 + (0 ^ ((lane >> 2) & 1))] = make_uint4(v8[0], v8[1], v8[2], v8[3]);
+    st4[lane * 2 + (1 ^ ((lane >> 2) & 1))] = make_uint4(v8[4], v8[5], v8[6], v8[7]);
+    __syncwarp();
+    const long long col0 = (long long)tn * BN + cbase + q * 8;
+    if (q + 1 < C8) {
+#pragma unroll
+      for (int it = 0; it < 2; ++it) nxt[it] = Epi::load4(args, row0 + 16 * it + (lane >> 1), col0 + 8 + 4 * (lane & 1));
+    }
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int rr = 16 * it + (lane >> 1);
+      const int qq = lane & 1;
+      const uint4 v = st4[rr * 2 + (qq ^ ((rr >> 2) & 1))];
+      if constexpr (INT8) {
+        Epi::apply4(args, row0 + rr, col0 + 4 * qq, make_int4((int)v.x, (int)v.y, (int)v.z, (int)v.w), cur[it]);
+      } else {
+        Epi::apply4(args, row0 + rr, col0 + 4 * qq,
+                    make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w)),
+                    cur[it]);
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < 2; ++it) cur[it] = nxt[it];
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) bar_arrive_cluster(a.acc == 0 ? lead_tempty0 : lead_tempty1);
+  a.next();
+  return true;
+}
+
+// Bounded wait until *count reaches target (acquire at GPU scope), then a proxy fence so that
+// this thread's later TMA loads see what the counted writers stored. Gives up when the CTA
+// aborts, when any CTA has recorded a failure, or after the wall-clock budget.
+__device__ __forceinline__ bool wait_count(const unsigned* count, unsigned target, volatile int* abort_flag, int* status) {
+  unsigned long long start = 0;
+  for (uint32_t it = 0;; ++it) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(count) : "memory");
+    if (v >= target) {
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      return true;
+    }
+    if (*abort_flag || *reinterpret_cast<volatile int*>(status) != TGCB_STATUS_OK) return false;
+    __nanosleep(128);
+    if ((it & 63u) == 63u) {
+      const unsigned long long t = now_ns();
+      if (start == 0) {
+        start = t;
+      } else if (t - start > WAIT_BUDGET_NS) {
+        *abort_flag = 1;
+        tgcb_fail(status, TGCB_STATUS_TIMEOUT_PRODUCER);
+        return false;
+      }
+    }
+  }
+}
+
+// Threads of a chain CTA: one more warp, which publishes stored first-GEMM tiles.
+constexpr int CHAIN_THREADS = THREADS + 32;
+
+// The pair kernel. Sched lists each pair's work items; item t < G1::NUM_TILES is tile t of
+// G1, item G1::NUM_TILES + t tile t of G2. With a second GEMM (a chain), G2 reads G1's output
+// as its A operand. When the 16 epilogue warps of a CTA have stored their rows of a G1 tile
+// they arrive on a stored barrier (release, CTA scope) and go on; the signal warp waits there
+// and adds 1 to rows_done[row block] (release, GPU scope), so no epilogue warp waits for its
+// stores to drain. A producer loads A for a G2 tile of row block m only after rows_done[m]
+// holds G1::TILES_N * 2 (every tile of the block, both CTAs; acquire + proxy fence). The
+// stored and published barriers are double-buffered, so the epilogue runs at most two G1
+// tiles ahead of the signal warp. rows_done holds zeros when the kernel starts. Every pair
+// must be resident at once for the waits to end; the runtime checks that before the first
+// chain launch, and the waits are bounded all the same.
+template <bool INT8, class G1, class G2, class Sched>
+__device__ __forceinline__ void pair_body(const TgcbArgs& args, const TgcbTmaDesc* ta1, const TgcbTmaDesc* tb1,
+                                          const TgcbTmaDesc* ta2, const TgcbTmaDesc* tb2, unsigned* rows_done) {
+  constexpr bool CHAIN = G2::NUM_TILES > 0;
+  constexpr unsigned ROW_COUNT = (unsigned)G1::TILES_N * 2u;
+  constexpr int NTHREADS = CHAIN ? CHAIN_THREADS : THREADS;
 
   extern __shared__ unsigned char tgcb_smem_raw[];
   const uint32_t raw = smem_addr(tgcb_smem_raw);
   unsigned char* smem = tgcb_smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-  const uint32_t sA = smem_addr(smem);
-  const uint32_t sB = sA + P_STAGES * P_A_STAGE;
+  PairCta c;
+  c.sA = smem_addr(smem);
+  c.sB = c.sA + P_STAGES * P_A_STAGE;
   unsigned long long* bars = reinterpret_cast<unsigned long long*>(smem + P_STAGES * (P_A_STAGE + P_B_STAGE));
-  const uint32_t bar0 = smem_addr(bars);
-  auto full_bar = [&](int s) { return bar0 + 8u * s; };
-  auto empty_bar = [&](int s) { return bar0 + 8u * (P_STAGES + s); };
-  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * P_STAGES + a); };
-  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * P_STAGES + 2 + a); };
+  c.bar0 = smem_addr(bars);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * P_STAGES + 4);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  c.abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_rank();  // 0: the leader, which issues the MMAs
-  const uint32_t peer = rank ^ 1u;
+  c.rank = cluster_rank();  // 0: the leader, which issues the MMAs
   const int pair = blockIdx.x >> 1;
   const int pairs = gridDim.x >> 1;
 
-  if (blockDim.x != THREADS || (gridDim.x & 1u) != 0u) {
+  if (blockDim.x != NTHREADS || (gridDim.x & 1u) != 0u) {
     // both CTAs of every pair see the same launch shape, so both leave here together
     if (threadIdx.x == 0) tgcb_fail(args.status, TGCB_STATUS_BAD_LAUNCH);
     return;
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < P_STAGES; ++s) {
-      bar_init(full_bar(s), 1);
-      bar_init(empty_bar(s), 1);
+      bar_init(c.full_bar(s), 1);
+      bar_init(c.empty_bar(s), 1);
     }
     for (int a = 0; a < 2; ++a) {
-      bar_init(tfull_bar(a), 1);
-      bar_init(tempty_bar(a), 2 * EPI_WARPS);
+      bar_init(c.tfull_bar(a), 1);
+      bar_init(c.tempty_bar(a), 2 * EPI_WARPS);
+      if (CHAIN) {
+        bar_init(c.stored_bar(a), EPI_WARPS);
+        bar_init(c.published_bar(a), 1);
+      }
     }
-    *abort_flag = 0;
+    *c.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -139,147 +374,94 @@ __device__ __forceinline__ void gemm_body_pair(const TgcbArgs& args, const TgcbT
   __syncthreads();
   cluster_sync();  // the peer's barriers are initialised before anything signals them
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  c.tmem = *tmem_slot;
+  const int items = Sched::count(pair, pairs);
 
   if (warp == 0) {
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(ta)) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(tb)) : "memory");
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int tile = pair; tile < NUM_TILES; tile += pairs) {
-        const int tm = tile / TILES_N;
-        const int tn = tile % TILES_N;
-        const int arow = tm * 2 * BM + (int)rank * BM;      // this CTA's rows of A
-        const int bcol = tn * BN + (int)rank * (BN / 2);    // this CTA's columns of B
-        for (int kb = 0; kb < NUM_KB; ++kb) {
-          if (!bar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.status, TGCB_STATUS_TIMEOUT_PRODUCER)) goto producer_done;
-          const uint32_t lead_full = cluster_addr(full_bar(stage), 0);
-          if (rank == 0) bar_arrive_expect(full_bar(stage), PAIR_TX);
-          const uint32_t a_dst = sA + stage * P_A_STAGE;
-          const uint32_t b_dst = sB + stage * P_B_STAGE;
-          if (!A_MN) {
-            tma_load_2d_pair(a_dst, ta, kb * KB, arow, lead_full);
-          } else {
-#pragma unroll
-            for (int c = 0; c < BM * EB / ROW_BYTES; ++c)
-              tma_load_2d_pair(a_dst + c * (KB * ROW_BYTES), ta, arow + c * (ROW_BYTES / EB), kb * KB, lead_full);
-          }
-          if (!B_MN) {
-            tma_load_2d_pair(b_dst, tb, kb * KB, bcol, lead_full);
-          } else {
-#pragma unroll
-            for (int c = 0; c < (BN / 2) * EB / ROW_BYTES; ++c)
-              tma_load_2d_pair(b_dst + c * (KB * ROW_BYTES), tb, bcol + c * (ROW_BYTES / EB), kb * KB, lead_full);
-          }
-          if (++stage == P_STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(ta1)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(tb1)) : "memory");
+      if constexpr (CHAIN) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(ta2)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(tb2)) : "memory");
       }
-    producer_done:;
-    }
-  } else if (warp == 1) {
-    if (lane == 0 && rank == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
-      for (int tile = pair; tile < NUM_TILES; tile += pairs) {
-        if (!bar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag, args.status, TGCB_STATUS_TIMEOUT_MMA)) break;
-        tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(acc * BN);
-        bool ok = true;
-        for (int kb = 0; kb < NUM_KB; ++kb) {
-          if (!bar_wait(full_bar(stage), phase, abort_flag, args.status, TGCB_STATUS_TIMEOUT_MMA)) {
-            ok = false;
-            break;
+      StageRing r;
+      for (int i = 0; i < items; ++i) {
+        const int t = Sched::item(pair, pairs, i);
+        bool ok = false;
+        if (CHAIN && t >= G1::NUM_TILES) {
+          if constexpr (CHAIN) {
+            const int t2 = t - G1::NUM_TILES;
+            ok = wait_count(rows_done + t2 / G2::TILES_N, ROW_COUNT, c.abort_flag, args.status) &&
+                 produce_tile<INT8, G2>(c, args, ta2, tb2, t2, r);
           }
-          tc_fence_after();
-          const uint32_t a_base = sA + stage * P_A_STAGE;
-          const uint32_t b_base = sB + stage * P_B_STAGE;
-#pragma unroll
-          for (int k = 0; k < KSTEPS; ++k) {
-            const unsigned long long adesc = A_MN ? umma_desc(a_base + k * MMA_K * ROW_BYTES, KB * ROW_BYTES, MN_SBO, MN_LAYOUT)
-                                                  : umma_desc(a_base + k * 32, 16, 1024);
-            const unsigned long long bdesc = B_MN ? umma_desc(b_base + k * MMA_K * ROW_BYTES, KB * ROW_BYTES, MN_SBO, MN_LAYOUT)
-                                                  : umma_desc(b_base + k * 32, 16, 1024);
-            mma_pair<INT8>(d, adesc, bdesc, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
-          }
-          mma_commit_pair(cluster_addr(empty_bar(stage), 0));
-          mma_commit_pair(cluster_addr(empty_bar(stage), 1));
-          if (++stage == P_STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+        } else {
+          ok = produce_tile<INT8, G1>(c, args, ta1, tb1, t, r);
         }
         if (!ok) break;
-        mma_commit_pair(cluster_addr(tfull_bar(acc), 0));
-        mma_commit_pair(cluster_addr(tfull_bar(acc), 1));
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1u;
       }
     }
-  } else {
+  } else if (warp == 1) {
+    if (lane == 0 && c.rank == 0) {
+      StageRing r;
+      AccRing a;
+      for (int i = 0; i < items; ++i) {
+        const int t = Sched::item(pair, pairs, i);
+        bool ok = false;
+        if (CHAIN && t >= G1::NUM_TILES) {
+          if constexpr (CHAIN) ok = mma_tile<INT8, G2>(c, args, r, a);
+        } else {
+          ok = mma_tile<INT8, G1>(c, args, r, a);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp < 2 + EPI_WARPS) {
     const int ew = warp - 2;
     const int quad = warp & 3;
-    const int part = ew >> 2;
-    uint32_t* stage = reinterpret_cast<uint32_t*>(smem + P_STAGES * (P_A_STAGE + P_B_STAGE) + BAR_BYTES) + ew * STAGE_WORDS;
-    uint4* st4 = reinterpret_cast<uint4*>(stage);
-    const uint32_t lead_tempty0 = cluster_addr(tempty_bar(0), 0);
-    const uint32_t lead_tempty1 = cluster_addr(tempty_bar(1), 0);
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    constexpr int C8 = BN / 4 / 8;
-    const int cbase = part * (BN / 4);
-    for (int tile = pair; tile < NUM_TILES; tile += pairs) {
-      const int tm = tile / TILES_N;
-      const int tn = tile % TILES_N;
-      const long long row0 = (long long)tm * 2 * BM + (long long)rank * BM + quad * 32;
-      typename Epi::Loads4 cur[2], nxt[2];
-#pragma unroll
-      for (int it = 0; it < 2; ++it)
-        cur[it] = Epi::load4(args, row0 + 16 * it + (lane >> 1), (long long)tn * BN + cbase + 4 * (lane & 1));
-      bool ok = true;
-      if (lane == 0) ok = bar_wait(tfull_bar(acc), acc_phase, abort_flag, args.status, TGCB_STATUS_TIMEOUT_EPILOGUE);
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      if (!ok) break;
-      tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < C8; ++c) {
-        uint32_t r[8];
-        tmem_ld8(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + cbase + c * 8), r);
-        st4[lane * 2 + (0 ^ ((lane >> 2) & 1))] = make_uint4(r[0], r[1], r[2], r[3]);
-        st4[lane * 2 + (1 ^ ((lane >> 2) & 1))] = make_uint4(r[4], r[5], r[6], r[7]);
-        __syncwarp();
-        const long long col0 = (long long)tn * BN + cbase + c * 8;
-        if (c + 1 < C8) {
-#pragma unroll
-          for (int it = 0; it < 2; ++it) nxt[it] = Epi::load4(args, row0 + 16 * it + (lane >> 1), col0 + 8 + 4 * (lane & 1));
+    const int cbase = (ew >> 2) * (BN / 4);
+    uint4* st4 = reinterpret_cast<uint4*>(reinterpret_cast<uint32_t*>(smem + P_STAGES * (P_A_STAGE + P_B_STAGE) + BAR_BYTES) +
+                                          ew * STAGE_WORDS);
+    const uint32_t lead_tempty0 = cluster_addr(c.tempty_bar(0), 0);
+    const uint32_t lead_tempty1 = cluster_addr(c.tempty_bar(1), 0);
+    AccRing a;
+    int g = 0;  // first-GEMM tiles this warp has stored
+    for (int i = 0; i < items; ++i) {
+      const int t = Sched::item(pair, pairs, i);
+      if (CHAIN && t >= G1::NUM_TILES) {
+        if constexpr (CHAIN) {
+          if (!epilogue_tile<INT8, G2>(c, args, t - G1::NUM_TILES, a, st4, quad, cbase, lane, lead_tempty0, lead_tempty1)) break;
         }
-#pragma unroll
-        for (int it = 0; it < 2; ++it) {
-          const int rr = 16 * it + (lane >> 1);
-          const int qq = lane & 1;
-          const uint4 v = st4[rr * 2 + (qq ^ ((rr >> 2) & 1))];
-          if constexpr (INT8) {
-            Epi::apply4(args, row0 + rr, col0 + 4 * qq, make_int4((int)v.x, (int)v.y, (int)v.z, (int)v.w), cur[it]);
-          } else {
-            Epi::apply4(args, row0 + rr, col0 + 4 * qq,
-                        make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w)),
-                        cur[it]);
-          }
+      } else {
+        if (!epilogue_tile<INT8, G1>(c, args, t, a, st4, quad, cbase, lane, lead_tempty0, lead_tempty1)) break;
+        if constexpr (CHAIN) {
+          // this warp's rows of the tile are stored: hand them to the signal warp, once it has
+          // published the tile that used this barrier slot before
+          bool ok = true;
+          if (lane == 0 && g >= 2)
+            ok = bar_wait(c.published_bar(g & 1), (uint32_t)(((g >> 1) - 1) & 1), c.abort_flag, args.status,
+                          TGCB_STATUS_TIMEOUT_EPILOGUE);
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          if (!ok) break;
+          if (lane == 0) bar_arrive(c.stored_bar(g & 1));
+          ++g;
         }
-        __syncwarp();
-#pragma unroll
-        for (int it = 0; it < 2; ++it) cur[it] = nxt[it];
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) bar_arrive_cluster(acc == 0 ? lead_tempty0 : lead_tempty1);
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1u;
+    }
+  } else if constexpr (CHAIN) {
+    // the signal warp: for each first-GEMM tile of this pair, once this CTA's epilogue warps
+    // have stored it, count it in its row block's counter for the G2 producers of every pair
+    if (lane == 0) {
+      int g = 0;
+      for (int i = 0; i < items; ++i) {
+        const int t = Sched::item(pair, pairs, i);
+        if (t >= G1::NUM_TILES) continue;
+        if (!bar_wait(c.stored_bar(g & 1), (uint32_t)((g >> 1) & 1), c.abort_flag, args.status, TGCB_STATUS_TIMEOUT_EPILOGUE))
+          break;
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(rows_done + t / G1::TILES_N) : "memory");
+        bar_arrive(c.published_bar(g & 1));
+        ++g;
+      }
     }
   }
   tc_fence_before();
@@ -287,8 +469,27 @@ __device__ __forceinline__ void gemm_body_pair(const TgcbArgs& args, const TgcbT
   cluster_sync();  // neither CTA frees its tensor memory or leaves while the pair still uses it
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)TMEM_COLS));
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(c.tmem), "r"((uint32_t)TMEM_COLS));
   }
+}
+
+// One GEMM on SM pairs.
+template <int M, int N, int K, bool INT8, bool A_MN, bool B_MN, class Epi>
+__device__ __forceinline__ void gemm_body_pair(const TgcbArgs& args, const TgcbTmaDesc* ta, const TgcbTmaDesc* tb) {
+  using G = PairGemm<M, N, K, A_MN, B_MN, Epi>;
+  pair_body<INT8, G, NoGemm, RoundRobin<G::NUM_TILES>>(args, ta, tb, ta, tb, nullptr);
+}
+
+// Two GEMMs on SM pairs, the second reading the first's output as A, in one persistent launch.
+template <bool INT8, class G1, class G2, class Sched>
+__device__ __forceinline__ void gemm_chain_pair(const TgcbArgs& args, const TgcbTmaDesc* ta1, const TgcbTmaDesc* tb1,
+                                                const TgcbTmaDesc* ta2, const TgcbTmaDesc* tb2, unsigned* rows_done) {
+  static_assert(G1::M == G2::M && !G2::A_MN, "a chain's second GEMM reads the first one's rows as its A");
+  if (gridDim.x != 2u * Sched::PAIRS) {
+    if (threadIdx.x == 0) tgcb_fail(args.status, TGCB_STATUS_BAD_LAUNCH);
+    return;
+  }
+  pair_body<INT8, G1, G2, Sched>(args, ta1, tb1, ta2, tb2, rows_done);
 }
 
 }  // namespace tgcb_gemm

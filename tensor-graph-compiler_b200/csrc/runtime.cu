@@ -82,8 +82,13 @@ struct LaunchState {
   cudaKernel_t kernel = nullptr;
   const void* a_ptr = nullptr;
   const void* b_ptr = nullptr;
+  const void* a2_ptr = nullptr;
+  const void* b2_ptr = nullptr;
+  bool residency_checked = false;  // a chain: every pair can be resident at once
   alignas(64) CUtensorMap ta;
   alignas(64) CUtensorMap tb;
+  alignas(64) CUtensorMap ta2;
+  alignas(64) CUtensorMap tb2;
 };
 
 struct tgcb_plan {
@@ -217,14 +222,25 @@ int tgcb_plan_create(tgcb_module* m, const tgcb_launch_desc* launches, int n_lau
                     cudaGetErrorString(e));
       }
     }
-    for (const tgcb_operand_desc* od : {&ls.desc.a, &ls.desc.b}) {
-      if (!ls.desc.is_gemm) break;
+    if (ls.desc.is_gemm > 3) {
+      delete p;
+      return fail(TGCB_E_INVALID, "%s: unknown launch kind %u", ls.desc.kernel, ls.desc.is_gemm);
+    }
+    const int n_ops = ls.desc.is_gemm == 3 ? 4 : ls.desc.is_gemm ? 2 : 0;
+    const tgcb_operand_desc* ops[4] = {&ls.desc.a, &ls.desc.b, &ls.desc.a2, &ls.desc.b2};
+    for (int k = 0; k < n_ops; ++k) {
+      const tgcb_operand_desc* od = ops[k];
       if (od->input_index >= TGCB_MAX_INPUTS || (od->input_index < 0 && od->arena_offset + od->rows * od->cols *
                                                                                                  od->elem_bytes >
                                                                              arena_bytes)) {
         delete p;
         return fail(TGCB_E_INVALID, "operand of %s lies outside the arena or the input table", ls.desc.kernel);
       }
+    }
+    if (ls.desc.is_gemm == 3 && (ls.desc.counter_bytes == 0 || (ls.desc.counter_offset & 3u) != 0 ||
+                                 ls.desc.counter_offset + ls.desc.counter_bytes > arena_bytes)) {
+      delete p;
+      return fail(TGCB_E_INVALID, "the counters of chain %s lie outside the arena", ls.desc.kernel);
     }
   }
   *out = p;
@@ -282,10 +298,11 @@ int launch_one(DeviceState* st, LaunchState& ls, TgcbArgs& args, void* arena, co
   dim3 block(d.block[0], d.block[1], d.block[2]);
   cudaError_t e;
   if (d.is_gemm) {
-    const tgcb_operand_desc* ods[2] = {&d.a, &d.b};
-    const void** cached[2] = {&ls.a_ptr, &ls.b_ptr};
-    CUtensorMap* maps[2] = {&ls.ta, &ls.tb};
-    for (int k = 0; k < 2; ++k) {
+    const tgcb_operand_desc* ods[4] = {&d.a, &d.b, &d.a2, &d.b2};
+    const void** cached[4] = {&ls.a_ptr, &ls.b_ptr, &ls.a2_ptr, &ls.b2_ptr};
+    CUtensorMap* maps[4] = {&ls.ta, &ls.tb, &ls.ta2, &ls.tb2};
+    const int n_maps = d.is_gemm == 3 ? 4 : 2;
+    for (int k = 0; k < n_maps; ++k) {
       const tgcb_operand_desc& od = *ods[k];
       const void* base;
       if (od.input_index >= 0) {
@@ -300,9 +317,9 @@ int launch_one(DeviceState* st, LaunchState& ls, TgcbArgs& args, void* arena, co
         *cached[k] = base;
       }
     }
-    void* params[3] = {&args, &ls.ta, &ls.tb};
-    if (d.is_gemm == 2) {
-      // two-SM GEMM: clusters of two CTAs (an even grid)
+    void* params[5] = {&args, &ls.ta, &ls.tb, &ls.ta2, &ls.tb2};
+    if (d.is_gemm >= 2) {
+      // two-SM GEMM or chain: clusters of two CTAs (an even grid)
       if ((d.grid[0] & 1u) != 0u) return fail(TGCB_E_INVALID, "%s: a pair GEMM needs an even grid", d.kernel);
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = grid;
@@ -316,6 +333,21 @@ int launch_one(DeviceState* st, LaunchState& ls, TgcbArgs& args, void* arena, co
       attr[0].val.clusterDim.z = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
+      if (d.is_gemm == 3) {
+        // A chain's second-GEMM tiles wait for first-GEMM tiles of other pairs, so all pairs
+        // must fit on the device together.
+        if (!ls.residency_checked) {
+          int clusters = 0;
+          e = cudaOccupancyMaxActiveClusters(&clusters, reinterpret_cast<const void*>(ls.kernel), &cfg);
+          if (e != cudaSuccess) return fail(TGCB_E_CUDA, "cluster occupancy of %s: %s", d.kernel, cudaGetErrorString(e));
+          if ((unsigned)clusters < d.grid[0] / 2)
+            return fail(TGCB_E_INVALID, "%s needs %u resident SM pairs, the device holds %d", d.kernel, d.grid[0] / 2,
+                        clusters);
+          ls.residency_checked = true;
+        }
+        e = cudaMemsetAsync(static_cast<char*>(arena) + d.counter_offset, 0, d.counter_bytes, s);
+        if (e != cudaSuccess) return fail(TGCB_E_CUDA, "zeroing the counters of %s: %s", d.kernel, cudaGetErrorString(e));
+      }
       e = cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(ls.kernel), params);
     } else {
       e = cudaLaunchKernel(reinterpret_cast<const void*>(ls.kernel), grid, block, params, d.smem_bytes, s);

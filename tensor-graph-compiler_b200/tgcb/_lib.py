@@ -49,6 +49,10 @@ class LaunchDesc(ctypes.Structure):
         ("is_gemm", ctypes.c_uint32),
         ("a", OperandDesc),
         ("b", OperandDesc),
+        ("a2", OperandDesc),
+        ("b2", OperandDesc),
+        ("counter_offset", ctypes.c_uint64),
+        ("counter_bytes", ctypes.c_uint64),
     ]
 
 

@@ -44,9 +44,12 @@ from tgcb.expr import ExprBuilder, _broadcast_index, contract_fma, ctype, deline
 
 NUM_SMS = 148
 PAIR_GEMM = True  # whole 256 x 256 tiles run on SM pairs
+CHAIN_GEMM = True  # two consecutive SM-pair GEMMs, the second reading the first's rows, share one launch
+CHAIN_MAX_ITEMS = 32768  # tiles of both GEMMs together (the schedule is a __constant__ table)
 _LOAD_LINE = re.compile(r"^\s*const (.+?) (ld_\d+) = (.*);$")
 _LOAD_NAME = re.compile(r"\b(ld_\d+)\b")
 GEMM_THREADS = 576  # tgcb_gemm::THREADS: TMA warp, MMA warp, 16 epilogue warps
+CHAIN_THREADS = GEMM_THREADS + 32  # tgcb_gemm::CHAIN_THREADS: plus the warp that publishes stored rows
 
 # Placeholder for the base pointer of a materialised value; replaced once the plan exists.
 def PTR(name: str) -> str:
@@ -70,6 +73,11 @@ class Launch:
     smem: int = 0
     gemm: tuple[GemmOperand, GemmOperand] | None = None
     pair: bool = False  # two-SM GEMM: launched as clusters of two CTAs
+    # a chain of two SM-pair GEMMs in one launch: the second GEMM's operands, and the arena
+    # value holding its per-row-block counters (zeroed before every launch)
+    gemm2: tuple[GemmOperand, GemmOperand] | None = None
+    counters: str | None = None
+    counter_bytes: int = 0
 
 
 @dataclass
@@ -82,6 +90,21 @@ class Step:
     launches: list[Launch] = field(default_factory=list)
     bracketing: str = ""
     nodes: list[str] = field(default_factory=list)
+    pair_gemm: PairGemmInfo | None = None  # set on an SM-pair GEMM step (chain fusion reads it)
+
+
+@dataclass
+class PairGemmInfo:
+    """What chain fusion needs from an SM-pair GEMM step."""
+
+    M: int
+    N: int
+    K: int
+    is_int: bool
+    opa: GemmOperand
+    opb: GemmOperand
+    epi_name: str
+    epi_source: str
 
 
 @dataclass
@@ -414,8 +437,96 @@ class Lowering:
             for st in new:
                 st.reads = sorted(set(st.reads) | self._step_reads)
             steps.extend(new)
+        if CHAIN_GEMM:
+            steps = self._fuse_chains(steps)
         self.steps = steps
         return steps
+
+    # ------------------------------------------------------------------ gemm chains
+
+    def _chainable(self, first: Step, second: Step) -> bool:
+        """Whether ``second`` may share ``first``'s launch as the second GEMM of a chain."""
+        g1, g2 = first.pair_gemm, second.pair_gemm
+        if g1 is None or g2 is None or g1.is_int != g2.is_int or g1.M != g2.M:
+            return False
+        a2 = g2.opa
+        # the second GEMM's A is the first one's stored output, read whole and K-major
+        if a2.value not in first.writes or a2.mn_major or (a2.rows, a2.cols) != (g1.M, g1.N):
+            return False
+        # nothing else of the second GEMM (B, epilogue side inputs) may come from the first
+        if g2.opb.value in first.writes or (set(second.reads) - {a2.value}) & set(first.writes):
+            return False
+        tiles = (g1.M // 256) * (g1.N // 256) + (g2.M // 256) * (g2.N // 256)
+        return tiles <= CHAIN_MAX_ITEMS
+
+    def _fuse_chains(self, steps: list[Step]) -> list[Step]:
+        out: list[Step] = []
+        i = 0
+        while i < len(steps):
+            if i + 1 < len(steps) and self._chainable(steps[i], steps[i + 1]):
+                out.append(self._chain_step(steps[i], steps[i + 1]))
+                i += 2
+            else:
+                out.append(steps[i])
+                i += 1
+        return out
+
+    def _chain_step(self, first: Step, second: Step) -> Step:
+        from tgcb import chain
+
+        g1, g2 = first.pair_gemm, second.pair_gemm
+        pairs = NUM_SMS // 2
+        kb_elems = 128 if g1.is_int else 32  # K values per 128-byte k-block
+        rows = g1.M // 256
+        tn1, tn2 = g1.N // 256, g2.N // 256
+        lists, _ = chain.schedule(rows * tn1, tn1, -(-g1.K // kb_elems), rows * tn2, tn2, -(-g2.K // kb_elems), pairs)
+        kname = self._kname("chain")
+        counters = f"{kname}_rows_done"
+        self.scratch[counters] = rows * 4
+        items = [t for lst in lists for t in lst]
+        offs = [0]
+        for lst in lists:
+            offs.append(offs[-1] + len(lst))
+
+        def table(name: str, vals: list[int]) -> str:
+            body = ", ".join(str(v) for v in vals)
+            return f"static __constant__ unsigned short {name}[{len(vals)}] = {{{body}}};\n"
+
+        sched = f"Sched_{kname}"
+        b = "true" if g1.is_int else "false"
+
+        def gemm_t(g: PairGemmInfo) -> str:
+            return (f"tgcb_gemm::PairGemm<{g.M}, {g.N}, {g.K}, {'true' if g.opa.mn_major else 'false'}, "
+                    f"{'true' if g.opb.mn_major else 'false'}, {g.epi_name}>")
+
+        source = (
+            g1.epi_source + g2.epi_source
+            + table(f"{kname}_items", items) + table(f"{kname}_first", offs)
+            + f"struct {sched} {{\n"
+            f"  static constexpr int PAIRS = {pairs};\n"
+            f"  static __device__ __forceinline__ int count(int pair, int) {{ return {kname}_first[pair + 1] - {kname}_first[pair]; }}\n"
+            f"  static __device__ __forceinline__ int item(int pair, int, int i) {{ return {kname}_items[{kname}_first[pair] + i]; }}\n"
+            "};\n"
+            f'extern "C" __global__ void __launch_bounds__({CHAIN_THREADS}, 1) {kname}(const TgcbArgs args, '
+            "const __grid_constant__ TgcbTmaDesc ta, const __grid_constant__ TgcbTmaDesc tb, "
+            "const __grid_constant__ TgcbTmaDesc ta2, const __grid_constant__ TgcbTmaDesc tb2) {\n"
+            f"  tgcb_gemm::gemm_chain_pair<{b}, {gemm_t(g1)}, {gemm_t(g2)}, {sched}>(args, &ta, &tb, &ta2, &tb2, "
+            f"reinterpret_cast<unsigned*>({PTR(counters)}));\n}}\n"
+        )
+        launch = Launch(kname, (2 * pairs, 1, 1), (CHAIN_THREADS, 1, 1), smem=-1, gemm=(g1.opa, g1.opb), pair=True,
+                        gemm2=(g2.opa, g2.opb), counters=counters, counter_bytes=rows * 4)
+        how = (f"{first.bracketing} | then {second.bracketing} | both GEMMs in one launch: {len(items)} tiles on "
+               f"{pairs} SM pairs in a fixed per-pair order, a tile of the second GEMM after its 256-row block of the first")
+        return Step(
+            "gemm",
+            f"{first.label}+{second.label}",
+            reads=sorted(set(first.reads) | set(second.reads)),
+            writes=list(first.writes) + [w for w in second.writes if w not in first.writes] + [counters],
+            source=source,
+            launches=[launch],
+            bracketing=how,
+            nodes=list(first.nodes) + list(second.nodes),
+        )
 
     def _row_shapes(self, src_sizes) -> list[tuple[int, ...]]:
         lead = tuple(src_sizes[:-1])
@@ -950,6 +1061,7 @@ class Lowering:
             if pair:
                 how += "; SM pairs (cta_group::2), 256 x 256 tiles"
         else:
+            pair = False
             kernel = self._gemm_simt_kernel(kname, epi_name, M, N, K, is_int, a_base, a_flip, b_base, b_flip)
             launch = Launch(kname, ((M * ((N + 15) // 16) + 127) // 128, 1, 1), (128, 1, 1))
             how = "SIMT fallback for rows TMA cannot tile: sequential over K with tf32-truncated operands"
@@ -962,6 +1074,7 @@ class Lowering:
             launches=[launch],
             bracketing=how,
             nodes=[name] + list(requests),
+            pair_gemm=PairGemmInfo(M, N, K, is_int, opa, opb, epi_name, epi) if pair else None,
         )
 
     def _gemm_vec4_epilogue(self, name: str, stores: list[str], M: int, N: int, acc_t: str,

@@ -230,11 +230,16 @@ def generate(graph, *, pipeline=None, optimise: bool = True) -> tuple:
             d.block = (ctypes.c_uint32 * 3)(*ln.block)
             if ln.gemm is not None:
                 # 1: one-SM kernel; 2: two-SM kernel, launched as clusters of two CTAs, each of
-                # which stages 128 columns of B
-                d.is_gemm = 2 if ln.pair else 1
+                # which stages 128 columns of B; 3: a chain of two two-SM GEMMs in one launch
+                d.is_gemm = 3 if ln.gemm2 is not None else 2 if ln.pair else 1
                 d.smem_bytes = GEMM_PAIR_SMEM if ln.pair else GEMM_SMEM
                 d.a = _operand_desc(ln.gemm[0], lowering, offsets, 128)
                 d.b = _operand_desc(ln.gemm[1], lowering, offsets, 128 if ln.pair else 256)
+                if ln.gemm2 is not None:
+                    d.a2 = _operand_desc(ln.gemm2[0], lowering, offsets, 128)
+                    d.b2 = _operand_desc(ln.gemm2[1], lowering, offsets, 128)
+                    d.counter_offset = offsets[ln.counters]
+                    d.counter_bytes = ln.counter_bytes
             else:
                 d.is_gemm = 0
                 d.smem_bytes = max(0, ln.smem)

@@ -8,7 +8,7 @@ import os
 import pytest
 from conftest import GOLDEN
 
-from tgcb import ir, memory, runtime, serialize, workloads
+from tgcb import codegen, ir, memory, runtime, serialize, workloads
 from tgcb.codegen import row_threads
 from tgcb.errors import CodegenError
 
@@ -30,7 +30,8 @@ def test_cone_is_one_row_kernel():
     assert set(mod.steps[0].writes) == set(low.outputs)
 
 
-def test_mlp_is_layernorm_then_two_gemms():
+def test_mlp_is_layernorm_then_two_gemms(monkeypatch):
+    monkeypatch.setattr(codegen, "CHAIN_GEMM", False)
     _, _, plan, mod, low = runtime.generate(workloads.mlp_graph(ir.Builder))
     assert [s.kind for s in mod.steps] == ["row", "gemm", "gemm"]
     ln, g1, g2 = mod.steps
@@ -40,6 +41,24 @@ def test_mlp_is_layernorm_then_two_gemms():
     assert "tgcb_gemm::gemm_body_pair<8192, 4096, 1024, false, false, true" in g1.source
     assert "tgcb_gemm::gemm_body_pair<8192, 1024, 4096, false, false, true" in g2.source
     assert all(ln.pair and ln.grid[0] % 2 == 0 for ln in g1.launches + g2.launches)
+
+
+def test_mlp_gemms_share_one_chain_launch():
+    _, _, plan, mod, low = runtime.generate(workloads.mlp_graph(ir.Builder))
+    assert [s.kind for s in mod.steps] == ["row", "gemm"]
+    ln, ch = mod.steps
+    (launch,) = ch.launches
+    assert launch.pair and launch.gemm2 is not None and launch.grid == (2 * codegen.NUM_SMS // 2, 1, 1)
+    assert "tgcb_tanh_approx" in ch.source
+    assert ("gemm_chain_pair<false, tgcb_gemm::PairGemm<8192, 4096, 1024, false, true, Epi_tgcb_gemm_2>, "
+            "tgcb_gemm::PairGemm<8192, 1024, 4096, false, true, Epi_tgcb_gemm_3>") in ch.source
+    # the hidden activation is the second GEMM's A operand; the counters (one per 256-row
+    # block) get an arena slot of their own, zeroed by the runtime before each launch
+    assert launch.gemm2[0].value in ch.writes and not launch.gemm2[0].mn_major
+    assert launch.counters in ch.writes and launch.counter_bytes == 8192 // 256 * 4
+    assert launch.counters in mod.offsets
+    desc = mod.launches[-1]
+    assert desc.is_gemm == 3 and desc.counter_bytes == 128 and desc.counter_offset % 4 == 0
 
 
 def test_int8_linear_is_one_int8_gemm_with_fused_dequant():
@@ -54,7 +73,9 @@ def test_gradient_graph_lowers():
     g = load_graph("train_grad_8192")
     mod = runtime.generate(g)[3]
     ks = [s.kind for s in mod.steps]
-    assert ks.count("gemm") == 5
+    # five GEMMs; the forward pair (x1 @ W1 then h @ W2) shares one chain launch
+    assert sum(2 if ln.gemm2 is not None else 1 for s in mod.steps for ln in s.launches if ln.gemm) == 5
+    assert ks.count("gemm") == 4
     assert ks.count("colreduce") == 2
     # transposes are absorbed as operand majors, never materialised
     assert all("transpose" not in s.kind for s in mod.steps)
