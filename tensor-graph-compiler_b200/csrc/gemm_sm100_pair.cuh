@@ -98,6 +98,13 @@ struct NoGemm {
   static constexpr int TILES_N = 1;
 };
 
+// Stands for "no row prologue" in pair_body. A row prologue (generated) computes the rows of the
+// first GEMM's A operand, one warp per row: GROUPS groups of EPI_WARPS rows, row(args, r, lane).
+struct NoRows {
+  static constexpr int GROUPS = 0;
+  static __device__ __forceinline__ void row(const TgcbArgs&, long long, int) {}
+};
+
 // The tiles of one GEMM dealt round-robin over the pairs (tile = pair + i * pairs).
 template <int NUM_TILES>
 struct RoundRobin {
@@ -116,7 +123,8 @@ struct PairCta {
   __device__ __forceinline__ uint32_t tfull_bar(int a) const { return bar0 + 8u * (2 * P_STAGES + a); }
   __device__ __forceinline__ uint32_t tempty_bar(int a) const { return bar0 + 8u * (2 * P_STAGES + 2 + a); }
   // chains only (index 2 * P_STAGES + 4 holds the tensor-memory address and the abort flag):
-  // the epilogue warps have stored a first-GEMM tile / the signal warp has published it
+  // the epilogue warps have stored a first-GEMM tile or prologue rows / the signal warp has
+  // published them
   __device__ __forceinline__ uint32_t stored_bar(int s) const { return bar0 + 8u * (2 * P_STAGES + 5 + s); }
   __device__ __forceinline__ uint32_t published_bar(int s) const { return bar0 + 8u * (2 * P_STAGES + 7 + s); }
 };
@@ -305,7 +313,32 @@ __device__ __forceinline__ bool wait_count(const unsigned* count, unsigned targe
   }
 }
 
-// Threads of a chain CTA: one more warp, which publishes stored first-GEMM tiles.
+// Epilogue side of the ev-th publish event of a CTA (one call per epilogue warp, after the
+// warp's stores): wait until the signal warp has published the event that used this barrier
+// slot two events ago, then arrive on the slot's stored barrier (release, CTA scope).
+__device__ __forceinline__ bool hand_over(const PairCta& c, const TgcbArgs& args, int ev, int lane) {
+  __syncwarp();
+  bool ok = true;
+  if (lane == 0 && ev >= 2)
+    ok = bar_wait(c.published_bar(ev & 1), (uint32_t)(((ev >> 1) - 1) & 1), c.abort_flag, args.status,
+                  TGCB_STATUS_TIMEOUT_EPILOGUE);
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  if (ok && lane == 0) bar_arrive(c.stored_bar(ev & 1));
+  return ok;
+}
+
+// Signal side of the ev-th publish event: once every epilogue warp has arrived, add 1 to
+// *counter (release, GPU scope: the warps' stores become visible to an acquiring reader on
+// any SM) and free the barrier slot.
+__device__ __forceinline__ bool publish(const PairCta& c, const TgcbArgs& args, int ev, unsigned* counter) {
+  if (!bar_wait(c.stored_bar(ev & 1), (uint32_t)((ev >> 1) & 1), c.abort_flag, args.status, TGCB_STATUS_TIMEOUT_EPILOGUE))
+    return false;
+  asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
+  bar_arrive(c.published_bar(ev & 1));
+  return true;
+}
+
+// Threads of a chain CTA: one more warp, which publishes stored rows.
 constexpr int CHAIN_THREADS = THREADS + 32;
 
 // The pair kernel. Sched lists each pair's work items; item t < G1::NUM_TILES is tile t of
@@ -316,15 +349,28 @@ constexpr int CHAIN_THREADS = THREADS + 32;
 // stores to drain. A producer loads A for a G2 tile of row block m only after rows_done[m]
 // holds G1::TILES_N * 2 (every tile of the block, both CTAs; acquire + proxy fence). The
 // stored and published barriers are double-buffered, so the epilogue runs at most two G1
-// tiles ahead of the signal warp. rows_done holds zeros when the kernel starts. Every pair
-// must be resident at once for the waits to end; the runtime checks that before the first
-// chain launch, and the waits are bounded all the same.
-template <bool INT8, class G1, class G2, class Sched>
+// tiles ahead of the signal warp.
+//
+// With a row prologue (Pro), G1's A operand is itself computed in this launch: before their
+// first tile the epilogue warps of CTA b compute row groups b, b + gridDim.x, ... (one row per
+// warp, Pro::row), each published like a G1 tile into rows_ready[row block] (rows_done +
+// G1::TILES_M), and a producer loads A for a G1 tile of row block m only after all
+// 2 * BM / EPI_WARPS groups of the block are counted.
+//
+// The counters hold zeros when the kernel starts. Every pair must be resident at once for the
+// waits to end; the runtime checks that before the first chain launch, and the waits are
+// bounded all the same.
+template <bool INT8, class G1, class G2, class Sched, class Pro = NoRows>
 __device__ __forceinline__ void pair_body(const TgcbArgs& args, const TgcbTmaDesc* ta1, const TgcbTmaDesc* tb1,
                                           const TgcbTmaDesc* ta2, const TgcbTmaDesc* tb2, unsigned* rows_done) {
   constexpr bool CHAIN = G2::NUM_TILES > 0;
+  constexpr bool PRO = Pro::GROUPS > 0;
+  constexpr bool SIGNAL = CHAIN || PRO;  // a signal warp publishes stored rows
   constexpr unsigned ROW_COUNT = (unsigned)G1::TILES_N * 2u;
-  constexpr int NTHREADS = CHAIN ? CHAIN_THREADS : THREADS;
+  constexpr unsigned GROUP_COUNT = (unsigned)(2 * BM / EPI_WARPS);  // row groups per 256-row block
+  constexpr int NTHREADS = SIGNAL ? CHAIN_THREADS : THREADS;
+  static_assert(!PRO || Pro::GROUPS * EPI_WARPS == G1::M, "a row prologue computes every row of G1's A");
+  unsigned* rows_ready = rows_done + G1::TILES_M;
 
   extern __shared__ unsigned char tgcb_smem_raw[];
   const uint32_t raw = smem_addr(tgcb_smem_raw);
@@ -356,7 +402,7 @@ __device__ __forceinline__ void pair_body(const TgcbArgs& args, const TgcbTmaDes
     for (int a = 0; a < 2; ++a) {
       bar_init(c.tfull_bar(a), 1);
       bar_init(c.tempty_bar(a), 2 * EPI_WARPS);
-      if (CHAIN) {
+      if (SIGNAL) {
         bar_init(c.stored_bar(a), EPI_WARPS);
         bar_init(c.published_bar(a), 1);
       }
@@ -396,7 +442,8 @@ __device__ __forceinline__ void pair_body(const TgcbArgs& args, const TgcbTmaDes
                  produce_tile<INT8, G2>(c, args, ta2, tb2, t2, r);
           }
         } else {
-          ok = produce_tile<INT8, G1>(c, args, ta1, tb1, t, r);
+          ok = (!PRO || wait_count(rows_ready + t / G1::TILES_N, GROUP_COUNT, c.abort_flag, args.status)) &&
+               produce_tile<INT8, G1>(c, args, ta1, tb1, t, r);
         }
         if (!ok) break;
       }
@@ -425,8 +472,15 @@ __device__ __forceinline__ void pair_body(const TgcbArgs& args, const TgcbTmaDes
     const uint32_t lead_tempty0 = cluster_addr(c.tempty_bar(0), 0);
     const uint32_t lead_tempty1 = cluster_addr(c.tempty_bar(1), 0);
     AccRing a;
-    int g = 0;  // first-GEMM tiles this warp has stored
-    for (int i = 0; i < items; ++i) {
+    int ev = 0;  // stores this warp has handed to the signal warp
+    bool ok = true;
+    if constexpr (PRO) {
+      for (int q = blockIdx.x; q < Pro::GROUPS; q += gridDim.x) {
+        Pro::row(args, (long long)q * EPI_WARPS + ew, lane);
+        if (!(ok = hand_over(c, args, ev++, lane))) break;
+      }
+    }
+    for (int i = 0; ok && i < items; ++i) {
       const int t = Sched::item(pair, pairs, i);
       if (CHAIN && t >= G1::NUM_TILES) {
         if constexpr (CHAIN) {
@@ -434,33 +488,24 @@ __device__ __forceinline__ void pair_body(const TgcbArgs& args, const TgcbTmaDes
         }
       } else {
         if (!epilogue_tile<INT8, G1>(c, args, t, a, st4, quad, cbase, lane, lead_tempty0, lead_tempty1)) break;
-        if constexpr (CHAIN) {
-          // this warp's rows of the tile are stored: hand them to the signal warp, once it has
-          // published the tile that used this barrier slot before
-          bool ok = true;
-          if (lane == 0 && g >= 2)
-            ok = bar_wait(c.published_bar(g & 1), (uint32_t)(((g >> 1) - 1) & 1), c.abort_flag, args.status,
-                          TGCB_STATUS_TIMEOUT_EPILOGUE);
-          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-          if (!ok) break;
-          if (lane == 0) bar_arrive(c.stored_bar(g & 1));
-          ++g;
-        }
+        if constexpr (CHAIN) ok = hand_over(c, args, ev++, lane);  // this warp's rows of the tile are stored
       }
     }
-  } else if constexpr (CHAIN) {
-    // the signal warp: for each first-GEMM tile of this pair, once this CTA's epilogue warps
-    // have stored it, count it in its row block's counter for the G2 producers of every pair
+  } else if constexpr (SIGNAL) {
+    // the signal warp: for each row group of the prologue and each first-GEMM tile of this
+    // CTA, once the epilogue warps have stored it, count it for the producers of every pair
     if (lane == 0) {
-      int g = 0;
-      for (int i = 0; i < items; ++i) {
-        const int t = Sched::item(pair, pairs, i);
-        if (t >= G1::NUM_TILES) continue;
-        if (!bar_wait(c.stored_bar(g & 1), (uint32_t)((g >> 1) & 1), c.abort_flag, args.status, TGCB_STATUS_TIMEOUT_EPILOGUE))
-          break;
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(rows_done + t / G1::TILES_N) : "memory");
-        bar_arrive(c.published_bar(g & 1));
-        ++g;
+      int ev = 0;
+      bool ok = true;
+      if constexpr (PRO) {
+        for (int q = blockIdx.x; ok && q < Pro::GROUPS; q += gridDim.x)
+          ok = publish(c, args, ev++, rows_ready + q * EPI_WARPS / (2 * BM));
+      }
+      if constexpr (CHAIN) {
+        for (int i = 0; ok && i < items; ++i) {
+          const int t = Sched::item(pair, pairs, i);
+          if (t < G1::NUM_TILES) ok = publish(c, args, ev++, rows_done + t / G1::TILES_N);
+        }
       }
     }
   }
@@ -481,15 +526,18 @@ __device__ __forceinline__ void gemm_body_pair(const TgcbArgs& args, const TgcbT
 }
 
 // Two GEMMs on SM pairs, the second reading the first's output as A, in one persistent launch.
-template <bool INT8, class G1, class G2, class Sched>
+// With Pro, the rows of the first GEMM's A operand are computed in the same launch. `counters`
+// holds G1::TILES_M words for the second GEMM's waits, then (with Pro) as many for the first's.
+template <bool INT8, class G1, class G2, class Sched, class Pro = NoRows>
 __device__ __forceinline__ void gemm_chain_pair(const TgcbArgs& args, const TgcbTmaDesc* ta1, const TgcbTmaDesc* tb1,
-                                                const TgcbTmaDesc* ta2, const TgcbTmaDesc* tb2, unsigned* rows_done) {
+                                                const TgcbTmaDesc* ta2, const TgcbTmaDesc* tb2, unsigned* counters) {
   static_assert(G1::M == G2::M && !G2::A_MN, "a chain's second GEMM reads the first one's rows as its A");
+  static_assert(Pro::GROUPS == 0 || !G1::A_MN, "a row prologue writes the rows of a K-major A");
   if (gridDim.x != 2u * Sched::PAIRS) {
     if (threadIdx.x == 0) tgcb_fail(args.status, TGCB_STATUS_BAD_LAUNCH);
     return;
   }
-  pair_body<INT8, G1, G2, Sched>(args, ta1, tb1, ta2, tb2, rows_done);
+  pair_body<INT8, G1, G2, Sched, Pro>(args, ta1, tb1, ta2, tb2, counters);
 }
 
 }  // namespace tgcb_gemm

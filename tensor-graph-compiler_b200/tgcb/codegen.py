@@ -45,6 +45,11 @@ from tgcb.expr import ExprBuilder, _broadcast_index, contract_fma, ctype, deline
 NUM_SMS = 148
 PAIR_GEMM = True  # whole 256 x 256 tiles run on SM pairs
 CHAIN_GEMM = True  # two consecutive SM-pair GEMMs, the second reading the first's rows, share one launch
+ROW_PROLOGUE = True  # a one-warp-per-row step producing a chain's first A operand runs inside the chain
+# ... when each CTA's epilogue warps have at most this many row groups (16 rows each) to compute
+# before their first tile: the MLP block's 8192 rows are 4 rounds over 148 CTAs and gain 2.7%; the
+# training step's 65536 rows (28 rounds) kept the epilogue from its first accumulators and lost 0.8%
+ROW_PROLOGUE_MAX_ROUNDS = 4
 CHAIN_MAX_ITEMS = 32768  # tiles of both GEMMs together (the schedule is a __constant__ table)
 _LOAD_LINE = re.compile(r"^\s*const (.+?) (ld_\d+) = (.*);$")
 _LOAD_NAME = re.compile(r"\b(ld_\d+)\b")
@@ -91,6 +96,17 @@ class Step:
     bracketing: str = ""
     nodes: list[str] = field(default_factory=list)
     pair_gemm: PairGemmInfo | None = None  # set on an SM-pair GEMM step (chain fusion reads it)
+    row_body: RowBody | None = None  # set on a one-warp-per-row step (row prologue fusion reads it)
+
+
+@dataclass
+class RowBody:
+    """A row step's per-row code for 32 threads (``row``, ``tid``, ``live`` in scope)."""
+
+    lines: str
+    nred: int
+    rows: int
+    cols: int
 
 
 @dataclass
@@ -459,19 +475,39 @@ class Lowering:
         tiles = (g1.M // 256) * (g1.N // 256) + (g2.M // 256) * (g2.N // 256)
         return tiles <= CHAIN_MAX_ITEMS
 
+    def _prologue_ok(self, row: Step, first: Step, second: Step) -> bool:
+        """Whether ``row`` can run as the row prologue of the chain (first, second): it writes
+        the first GEMM's A operand whole, one warp per row, and nothing of what it writes is
+        read by the chain other than through that operand's TMA loads."""
+        body, a1 = row.row_body, first.pair_gemm.opa
+        if body is None or len(row.launches) != 1 or a1.value not in row.writes or a1.mn_major:
+            return False
+        if (a1.rows, a1.cols) != (body.rows, body.cols) or body.rows % 256:
+            return False
+        if -(-(body.rows // 16) // NUM_SMS) > ROW_PROLOGUE_MAX_ROUNDS:
+            return False
+        epis = first.pair_gemm.epi_source + second.pair_gemm.epi_source
+        for w in row.writes:
+            if PTR(w) in epis or w in (first.pair_gemm.opb.value, second.pair_gemm.opb.value):
+                return False
+        return all(w == a1.value or w not in second.reads for w in row.writes)
+
     def _fuse_chains(self, steps: list[Step]) -> list[Step]:
         out: list[Step] = []
         i = 0
         while i < len(steps):
             if i + 1 < len(steps) and self._chainable(steps[i], steps[i + 1]):
-                out.append(self._chain_step(steps[i], steps[i + 1]))
+                row = None
+                if ROW_PROLOGUE and out and self._prologue_ok(out[-1], steps[i], steps[i + 1]):
+                    row = out.pop()
+                out.append(self._chain_step(steps[i], steps[i + 1], row))
                 i += 2
             else:
                 out.append(steps[i])
                 i += 1
         return out
 
-    def _chain_step(self, first: Step, second: Step) -> Step:
+    def _chain_step(self, first: Step, second: Step, row: Step | None = None) -> Step:
         from tgcb import chain
 
         g1, g2 = first.pair_gemm, second.pair_gemm
@@ -482,7 +518,10 @@ class Lowering:
         lists, _ = chain.schedule(rows * tn1, tn1, -(-g1.K // kb_elems), rows * tn2, tn2, -(-g2.K // kb_elems), pairs)
         kname = self._kname("chain")
         counters = f"{kname}_rows_done"
-        self.scratch[counters] = rows * 4
+        # one counter per 256-row block for the second GEMM's waits, and with a row prologue as
+        # many for the first GEMM's
+        counter_bytes = rows * 4 * (2 if row is not None else 1)
+        self.scratch[counters] = counter_bytes
         items = [t for lst in lists for t in lst]
         offs = [0]
         for lst in lists:
@@ -499,8 +538,23 @@ class Lowering:
             return (f"tgcb_gemm::PairGemm<{g.M}, {g.N}, {g.K}, {'true' if g.opa.mn_major else 'false'}, "
                     f"{'true' if g.opb.mn_major else 'false'}, {g.epi_name}>")
 
+        pro = ""
+        pro_t = ""
+        if row is not None:
+            body = row.row_body
+            pro_t = f", Rows_{kname}"
+            pro = (
+                f"struct Rows_{kname} {{\n"
+                f"  static constexpr int GROUPS = {body.rows // 16};  // groups of tgcb_gemm::EPI_WARPS rows\n"
+                "  static __device__ __forceinline__ void row(const TgcbArgs& args, const long long row, const int tid) {\n"
+                f"    double red_smem[{body.nred}][1][1];  // one warp per row: never written\n"
+                "    const int grp = 0;\n"
+                "    const bool live = true;\n"
+                f"{body.lines}\n"
+                "  }\n};\n"
+            )
         source = (
-            g1.epi_source + g2.epi_source
+            g1.epi_source + g2.epi_source + pro
             + table(f"{kname}_items", items) + table(f"{kname}_first", offs)
             + f"struct {sched} {{\n"
             f"  static constexpr int PAIRS = {pairs};\n"
@@ -510,22 +564,31 @@ class Lowering:
             f'extern "C" __global__ void __launch_bounds__({CHAIN_THREADS}, 1) {kname}(const TgcbArgs args, '
             "const __grid_constant__ TgcbTmaDesc ta, const __grid_constant__ TgcbTmaDesc tb, "
             "const __grid_constant__ TgcbTmaDesc ta2, const __grid_constant__ TgcbTmaDesc tb2) {\n"
-            f"  tgcb_gemm::gemm_chain_pair<{b}, {gemm_t(g1)}, {gemm_t(g2)}, {sched}>(args, &ta, &tb, &ta2, &tb2, "
+            f"  tgcb_gemm::gemm_chain_pair<{b}, {gemm_t(g1)}, {gemm_t(g2)}, {sched}{pro_t}>(args, &ta, &tb, &ta2, &tb2, "
             f"reinterpret_cast<unsigned*>({PTR(counters)}));\n}}\n"
         )
         launch = Launch(kname, (2 * pairs, 1, 1), (CHAIN_THREADS, 1, 1), smem=-1, gemm=(g1.opa, g1.opb), pair=True,
-                        gemm2=(g2.opa, g2.opb), counters=counters, counter_bytes=rows * 4)
+                        gemm2=(g2.opa, g2.opb), counters=counters, counter_bytes=counter_bytes)
         how = (f"{first.bracketing} | then {second.bracketing} | both GEMMs in one launch: {len(items)} tiles on "
                f"{pairs} SM pairs in a fixed per-pair order, a tile of the second GEMM after its 256-row block of the first")
+        reads = set(first.reads) | set(second.reads)
+        writes = list(first.writes) + [w for w in second.writes if w not in first.writes] + [counters]
+        nodes = list(first.nodes) + list(second.nodes)
+        if row is not None:
+            how = (f"{row.bracketing}, the rows computed inside the launch by the epilogue warps (one warp per row) "
+                   f"before their first tile, a tile of the first GEMM after its 256 rows | " + how)
+            reads |= set(row.reads)
+            writes = list(row.writes) + [w for w in writes if w not in row.writes]
+            nodes = list(row.nodes) + nodes
         return Step(
             "gemm",
             f"{first.label}+{second.label}",
-            reads=sorted(set(first.reads) | set(second.reads)),
-            writes=list(first.writes) + [w for w in second.writes if w not in first.writes] + [counters],
+            reads=sorted(reads),
+            writes=writes,
             source=source,
             launches=[launch],
             bracketing=how,
-            nodes=list(first.nodes) + list(second.nodes),
+            nodes=nodes,
         )
 
     def _row_shapes(self, src_sizes) -> list[tuple[int, ...]]:
@@ -774,7 +837,7 @@ class Lowering:
             + "\n  }\n}\n"
         )
         writes = [m for m in members if m in self.materialised] + list(requests)
-        return Step(
+        step = Step(
             "row",
             ",".join(members),
             reads=sorted(reads),
@@ -785,6 +848,11 @@ class Lowering:
             f"lanes combined by xor tree (1,2,4,8,16); {W} warp partials combined as a balanced tree",
             nodes=list(members) + list(requests),
         )
+        if T == 32 and unrolled:
+            # one warp per row and no shared-memory partials: the same body can run inside a
+            # GEMM chain launch, one row per epilogue warp (a row prologue)
+            step.row_body = RowBody("\n".join(lines), nred, R, C)
+        return step
 
     def _reduction_steps(self, node) -> list[Step]:
         kind = self.reduction_kind(node)

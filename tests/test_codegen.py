@@ -43,7 +43,23 @@ def test_mlp_is_layernorm_then_two_gemms(monkeypatch):
     assert all(ln.pair and ln.grid[0] % 2 == 0 for ln in g1.launches + g2.launches)
 
 
-def test_mlp_gemms_share_one_chain_launch():
+def test_mlp_is_one_launch_with_the_layernorm_as_row_prologue():
+    _, _, plan, mod, low = runtime.generate(workloads.mlp_graph(ir.Builder))
+    assert [s.kind for s in mod.steps] == ["gemm"]
+    (ch,) = mod.steps
+    (launch,) = ch.launches
+    assert launch.gemm2 is not None and launch.block == (codegen.CHAIN_THREADS, 1, 1)
+    # the layernorm body runs one row per epilogue warp: 8192 rows in groups of 16
+    assert "struct Rows_tgcb_chain_4" in ch.source and "GROUPS = 512;" in ch.source
+    assert ", Rows_tgcb_chain_4>(args" in ch.source and "tgcb_row_1(" not in ch.source
+    # the normalised x is written and read inside the launch; counters for both GEMMs' waits
+    assert launch.gemm[0].value in ch.writes
+    assert launch.counter_bytes == 2 * (8192 // 256) * 4
+    assert "layernorm" in ch.bracketing or "row tree: 32 threads per row" in ch.bracketing
+
+
+def test_mlp_gemms_share_one_chain_launch(monkeypatch):
+    monkeypatch.setattr(codegen, "ROW_PROLOGUE", False)
     _, _, plan, mod, low = runtime.generate(workloads.mlp_graph(ir.Builder))
     assert [s.kind for s in mod.steps] == ["row", "gemm"]
     ln, ch = mod.steps

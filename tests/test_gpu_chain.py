@@ -98,3 +98,39 @@ def test_chain_on_two_arenas_and_streams(cuda, monkeypatch):
     for f, got in zip(fs, outs, strict=True):
         (want,) = interp.run(g, f)
         assert float((got.cpu().double() - want.double()).abs().max()) <= 5e-3 * float(want.double().abs().max())
+
+
+@pytest.mark.parametrize(
+    "rows,d,f",
+    [
+        (512, 256, 512),     # 32 row groups for 148 CTAs: most CTAs compute no rows
+        (2048, 256, 1024),
+        (8192, 1024, 4096),  # the MLP block
+    ],
+)
+def test_layernorm_prologue_is_bit_identical_to_its_own_launch(cuda, monkeypatch, rows, d, f):
+    # the layernorm rows computed by the chain's epilogue warps run the row kernel's code for
+    # one warp per row, so every output matches the separate row-kernel launch bit for bit
+    from tgcb import workloads
+
+    g = workloads.mlp_graph(ir.Builder, rows=rows, d=d, f=f)
+    f_in = workloads.mlp_inputs(rows=rows, d=d, f=f, seed=5)
+    outs = {}
+    for pro in (False, True):
+        monkeypatch.setattr(codegen, "ROW_PROLOGUE", pro)
+        monkeypatch.setattr(codegen, "CHAIN_GEMM", True)
+        c = compile_graph(g)
+        kinds = [s.kind for s in c.module.steps]
+        assert kinds == (["gemm"] if pro else ["row", "gemm"])
+        arena = c.new_arena()
+        for _ in range(2):  # the second call reuses the arena and the counters
+            got = [o.clone() for o in c.function(arena, {k: v.cuda() for k, v in f_in.items()})]
+        torch.cuda.synchronize()
+        c.check_status()
+        outs[pro] = got
+    for a, b in zip(outs[True], outs[False], strict=True):
+        assert torch.equal(a, b)
+    if rows <= 2048:
+        (want,) = interp.run(g, f_in)
+        got = outs[True][0].cpu().double()
+        assert float((got - want.double()).abs().max()) <= 5e-3 * float(want.double().abs().max())
