@@ -349,9 +349,14 @@ class GraphWorkload:
                     N = low.sizes(node.inputs[1])[1]
                     is_int = node.output.dtype.name == "int32"
                     work += 2 * M * N * K
+                # a chain launch may also compute its first GEMM's A rows (a row prologue); those
+                # bytes are not in the tensor-bound work
+                rows = [n for n in s.nodes if n in low.producers and low.producers[n].op.category == "reduction"]
+                also = (f"computes the rows of {', '.join(rows)} (row prologue) besides the GEMM FLOPs counted in achieved"
+                        if rows else None)
                 for ln in s.launches:
                     out.append({"name": ln.kernel, "kind": s.kind, "bound": "tensor", "work": work,
-                                "type": "int8" if is_int else "tf32"})
+                                "type": "int8" if is_int else "tf32", "also": also})
                 continue
             rbytes = sum(low.values[r].bytes for r in s.reads if r in low.values)
             wbytes = sum(low.values[w].bytes for w in s.writes if w in low.values)
@@ -992,6 +997,7 @@ def _main(json_out) -> int:
                 "frac": round(achieved / peak, 4),
                 "traffic": read_traffic(args.workload, dk["name"]),
                 "peak_source": peak_note,
+                **({"also": dk["also"]} if dk.get("also") else {}),
             },
             "hbm_kernels": {
                 "algorithmic_bytes_per_exec": hbm_bytes,
