@@ -62,10 +62,11 @@ typedef struct tgcb_operand_desc {
 /* One kernel launch of a plan. Plain kernels take TgcbArgs; GEMM kernels take TgcbArgs
  * and two tensor maps that tgcb_plan_run encodes from a and b; a chain (is_gemm 3: two GEMMs
  * in one launch of clusters of two CTAs, the second reading the first one's output rows) takes
- * four, from a, b, a2 and b2, and tgcb_plan_run zeroes its counter_bytes of arena at
- * counter_offset (per-row-block counters) before every launch. Every pair of a chain must be
- * resident at once: the first launch checks the device's cluster occupancy and fails with
- * TGCB_E_INVALID when it cannot hold them. */
+ * four, from a, b, a2 and b2. For any GEMM launch with counter_bytes > 0 (a chain's per-row-
+ * block counters, a K-split GEMM's per-region counters) tgcb_plan_run zeroes that many bytes of
+ * arena at counter_offset before every launch. Every pair of a chain must be resident at once:
+ * the first launch checks the device's cluster occupancy and fails with TGCB_E_INVALID when it
+ * cannot hold them. */
 typedef struct tgcb_launch_desc {
   char kernel[96];
   uint32_t grid[3];
@@ -76,8 +77,8 @@ typedef struct tgcb_launch_desc {
   tgcb_operand_desc b;
   tgcb_operand_desc a2;  /* is_gemm 3 only */
   tgcb_operand_desc b2;  /* is_gemm 3 only */
-  uint64_t counter_offset; /* is_gemm 3 only: bytes from the arena base, 4-byte aligned */
-  uint64_t counter_bytes;
+  uint64_t counter_offset; /* GEMM launches: bytes from the arena base, 4-byte aligned */
+  uint64_t counter_bytes;  /* 0: no counters (required > 0 for is_gemm 3) */
 } tgcb_launch_desc;
 
 /* Library version string. */

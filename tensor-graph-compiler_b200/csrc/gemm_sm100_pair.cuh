@@ -77,19 +77,23 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
 }
 
 // One GEMM run by the pair kernel: C[M,N] = A[M,K] @ B[K,N] and its generated epilogue.
-template <int M_, int N_, int K_, bool A_MN_, bool B_MN_, class Epi_>
+// With SPLIT > 1 the K range is cut into SPLIT equal slices and every (slice, output tile) is
+// a work item: item t is slice t / TILES of output tile t % TILES.
+template <int M_, int N_, int K_, bool A_MN_, bool B_MN_, class Epi_, int SPLIT_ = 1>
 struct PairGemm {
   static constexpr int M = M_;
   static constexpr int N = N_;
   static constexpr int K = K_;
   static constexpr bool A_MN = A_MN_;
   static constexpr bool B_MN = B_MN_;
+  static constexpr int SPLIT = SPLIT_;
   using Epi = Epi_;
   static_assert(Epi::VEC4, "the two-SM kernel uses the four-column epilogue");
   static_assert(M % (2 * BM) == 0 && N % BN == 0, "the two-SM kernel covers whole 256 x 256 tiles");
   static constexpr int TILES_M = M / (2 * BM);
   static constexpr int TILES_N = N / BN;
-  static constexpr int NUM_TILES = TILES_M * TILES_N;
+  static constexpr int TILES = TILES_M * TILES_N;  // output tiles
+  static constexpr int NUM_TILES = TILES * SPLIT;  // work items
 };
 
 // Stands for "no second GEMM" in pair_body.
@@ -158,12 +162,16 @@ __device__ __forceinline__ bool produce_tile(const PairCta& c, const TgcbArgs& a
   constexpr int EB = INT8 ? 1 : 4;
   constexpr int KB = ROW_BYTES / EB;
   constexpr int NUM_KB = (G::K + KB - 1) / KB;
+  constexpr int KB_PER = NUM_KB / G::SPLIT;  // k-blocks of one item
+  static_assert(NUM_KB % G::SPLIT == 0, "K splits into whole k-blocks");
   constexpr uint32_t PAIR_TX = 2 * (P_A_STAGE + P_B_STAGE);  // both CTAs' halves land on the leader's barrier
-  const int tm = tile / G::TILES_N;
-  const int tn = tile % G::TILES_N;
+  const int out = tile % G::TILES;
+  const int kb0 = (tile / G::TILES) * KB_PER;
+  const int tm = out / G::TILES_N;
+  const int tn = out % G::TILES_N;
   const int arow = tm * 2 * BM + (int)c.rank * BM;      // this CTA's rows of A
   const int bcol = tn * BN + (int)c.rank * (BN / 2);    // this CTA's columns of B
-  for (int kb = 0; kb < NUM_KB; ++kb) {
+  for (int kb = kb0; kb < kb0 + KB_PER; ++kb) {
     if (!bar_wait(c.empty_bar(r.stage), r.phase ^ 1u, c.abort_flag, args.status, TGCB_STATUS_TIMEOUT_PRODUCER)) return false;
     const uint32_t lead_full = cluster_addr(c.full_bar(r.stage), 0);
     if (c.rank == 0) bar_arrive_expect(c.full_bar(r.stage), PAIR_TX);
@@ -203,10 +211,11 @@ __device__ __forceinline__ bool mma_tile(const PairCta& c, const TgcbArgs& args,
   constexpr uint32_t IDESC = (INT8 ? (2u << 4) : (1u << 4)) | (INT8 ? (1u << 7) : (2u << 7)) |
                              (INT8 ? (1u << 10) : (2u << 10)) | ((G::A_MN ? 1u : 0u) << 15) |
                              ((G::B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
+  constexpr int KB_PER = NUM_KB / G::SPLIT;  // k-blocks of one item
   if (!bar_wait(c.tempty_bar(a.acc), a.phase ^ 1u, c.abort_flag, args.status, TGCB_STATUS_TIMEOUT_MMA)) return false;
   tc_fence_after();
   const uint32_t d = c.tmem + (uint32_t)(a.acc * BN);
-  for (int kb = 0; kb < NUM_KB; ++kb) {
+  for (int kb = 0; kb < KB_PER; ++kb) {
     if (!bar_wait(c.full_bar(r.stage), r.phase, c.abort_flag, args.status, TGCB_STATUS_TIMEOUT_MMA)) return false;
     tc_fence_after();
     const uint32_t a_base = c.sA + r.stage * P_A_STAGE;
@@ -233,23 +242,37 @@ __device__ __forceinline__ bool mma_tile(const PairCta& c, const TgcbArgs& args,
 // time out of tensor memory, transposed through shared memory so that two lanes hand one
 // row's four consecutive columns to the generated apply4; then the accumulator goes back to
 // the leader.
+//
+// A K-split item (G::SPLIT > 1) stores its partial accumulator instead, as slice s of the
+// workspace ws[SPLIT][M][N] (32-bit: float, or int for int8), and counts it in its region's
+// counter (region = CTA rank, lane quadrant and column quarter: the 32 x 64 block this warp
+// covers in every slice). The warp that counts the last slice of a region sums the SPLIT
+// partials of the region in slice order 0, 1, ... (the same order whichever slice finished
+// last) and runs apply4 on the sums: the result does not depend on timing.
 template <bool INT8, class G>
 __device__ __forceinline__ bool epilogue_tile(const PairCta& c, const TgcbArgs& args, int tile, AccRing& a, uint4* st4,
-                                              int quad, int cbase, int lane, uint32_t lead_tempty0, uint32_t lead_tempty1) {
+                                              int quad, int cbase, int lane, uint32_t lead_tempty0, uint32_t lead_tempty1,
+                                              void* ws, unsigned* counters) {
   using Epi = typename G::Epi;
   constexpr int C8 = BN / 4 / 8;
-  const int tm = tile / G::TILES_N;
-  const int tn = tile % G::TILES_N;
+  constexpr bool SPLIT = G::SPLIT > 1;
+  const int out = tile % G::TILES;
+  const int tm = out / G::TILES_N;
+  const int tn = out % G::TILES_N;
   const long long row0 = (long long)tm * 2 * BM + (long long)c.rank * BM + quad * 32;
   typename Epi::Loads4 cur[2], nxt[2];
+  if constexpr (!SPLIT) {
 #pragma unroll
-  for (int it = 0; it < 2; ++it)
-    cur[it] = Epi::load4(args, row0 + 16 * it + (lane >> 1), (long long)tn * BN + cbase + 4 * (lane & 1));
+    for (int it = 0; it < 2; ++it)
+      cur[it] = Epi::load4(args, row0 + 16 * it + (lane >> 1), (long long)tn * BN + cbase + 4 * (lane & 1));
+  }
   bool ok = true;
   if (lane == 0) ok = bar_wait(c.tfull_bar(a.acc), a.phase, c.abort_flag, args.status, TGCB_STATUS_TIMEOUT_EPILOGUE);
   ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
   if (!ok) return false;
   tc_fence_after();
+  uint4* slice = nullptr;
+  if constexpr (SPLIT) slice = reinterpret_cast<uint4*>(static_cast<uint32_t*>(ws) + (long long)(tile / G::TILES) * G::M * G::N);
 #pragma unroll 1
   for (int q = 0; q < C8; ++q) {
     uint32_t v8[8];
@@ -258,16 +281,20 @@ __device__ __forceinline__ bool epilogue_tile(const PairCta& c, const TgcbArgs& 
     st4[lane * 2 + (1 ^ ((lane >> 2) & 1))] = make_uint4(v8[4], v8[5], v8[6], v8[7]);
     __syncwarp();
     const long long col0 = (long long)tn * BN + cbase + q * 8;
-    if (q + 1 < C8) {
+    if constexpr (!SPLIT) {
+      if (q + 1 < C8) {
 #pragma unroll
-      for (int it = 0; it < 2; ++it) nxt[it] = Epi::load4(args, row0 + 16 * it + (lane >> 1), col0 + 8 + 4 * (lane & 1));
+        for (int it = 0; it < 2; ++it) nxt[it] = Epi::load4(args, row0 + 16 * it + (lane >> 1), col0 + 8 + 4 * (lane & 1));
+      }
     }
 #pragma unroll
     for (int it = 0; it < 2; ++it) {
       const int rr = 16 * it + (lane >> 1);
       const int qq = lane & 1;
       const uint4 v = st4[rr * 2 + (qq ^ ((rr >> 2) & 1))];
-      if constexpr (INT8) {
+      if constexpr (SPLIT) {
+        slice[((row0 + rr) * G::N + col0 + 4 * qq) >> 2] = v;  // the raw partial accumulator
+      } else if constexpr (INT8) {
         Epi::apply4(args, row0 + rr, col0 + 4 * qq, make_int4((int)v.x, (int)v.y, (int)v.z, (int)v.w), cur[it]);
       } else {
         Epi::apply4(args, row0 + rr, col0 + 4 * qq,
@@ -276,13 +303,60 @@ __device__ __forceinline__ bool epilogue_tile(const PairCta& c, const TgcbArgs& 
       }
     }
     __syncwarp();
+    if constexpr (!SPLIT) {
 #pragma unroll
-    for (int it = 0; it < 2; ++it) cur[it] = nxt[it];
+      for (int it = 0; it < 2; ++it) cur[it] = nxt[it];
+    }
   }
   tc_fence_before();
   __syncwarp();
   if (lane == 0) bar_arrive_cluster(a.acc == 0 ? lead_tempty0 : lead_tempty1);
   a.next();
+  if constexpr (SPLIT) {
+    // publish this slice of the region; the last of the SPLIT slices finishes the region
+    __threadfence();
+    __syncwarp();
+    unsigned seen = 0;
+    if (lane == 0) seen = atomicAdd(counters + out * 32 + (int)c.rank * 16 + (cbase / (BN / 4)) * 4 + quad, 1u);
+    seen = __shfl_sync(0xffffffffu, seen, 0);
+    if (seen == (unsigned)(G::SPLIT - 1)) {
+      __threadfence();
+      const uint4* base = reinterpret_cast<const uint4*>(ws);
+      constexpr long long SLICE = (long long)G::M * G::N / 4;
+#pragma unroll 1
+      for (int q = 0; q < C8; ++q) {
+        const long long col0 = (long long)tn * BN + cbase + q * 8;
+#pragma unroll
+        for (int it = 0; it < 2; ++it) {
+          const long long row = row0 + 16 * it + (lane >> 1);
+          const long long col = col0 + 4 * (lane & 1);
+          const long long e = (row * G::N + col) >> 2;
+          uint4 v = __ldcg(base + e);
+          if constexpr (INT8) {
+            int4 t = make_int4((int)v.x, (int)v.y, (int)v.z, (int)v.w);
+            for (int k = 1; k < G::SPLIT; ++k) {
+              const uint4 w = __ldcg(base + k * SLICE + e);
+              t.x += (int)w.x;
+              t.y += (int)w.y;
+              t.z += (int)w.z;
+              t.w += (int)w.w;
+            }
+            Epi::apply4(args, row, col, t, Epi::load4(args, row, col));
+          } else {
+            float4 t = make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w));
+            for (int k = 1; k < G::SPLIT; ++k) {
+              const uint4 w = __ldcg(base + k * SLICE + e);
+              t.x = __fadd_rn(t.x, __uint_as_float(w.x));
+              t.y = __fadd_rn(t.y, __uint_as_float(w.y));
+              t.z = __fadd_rn(t.z, __uint_as_float(w.z));
+              t.w = __fadd_rn(t.w, __uint_as_float(w.w));
+            }
+            Epi::apply4(args, row, col, t, Epi::load4(args, row, col));
+          }
+        }
+      }
+    }
+  }
   return true;
 }
 
@@ -362,7 +436,8 @@ constexpr int CHAIN_THREADS = THREADS + 32;
 // bounded all the same.
 template <bool INT8, class G1, class G2, class Sched, class Pro = NoRows>
 __device__ __forceinline__ void pair_body(const TgcbArgs& args, const TgcbTmaDesc* ta1, const TgcbTmaDesc* tb1,
-                                          const TgcbTmaDesc* ta2, const TgcbTmaDesc* tb2, unsigned* rows_done) {
+                                          const TgcbTmaDesc* ta2, const TgcbTmaDesc* tb2, unsigned* rows_done,
+                                          void* ws = nullptr) {
   constexpr bool CHAIN = G2::NUM_TILES > 0;
   constexpr bool PRO = Pro::GROUPS > 0;
   constexpr bool SIGNAL = CHAIN || PRO;  // a signal warp publishes stored rows
@@ -484,10 +559,11 @@ __device__ __forceinline__ void pair_body(const TgcbArgs& args, const TgcbTmaDes
       const int t = Sched::item(pair, pairs, i);
       if (CHAIN && t >= G1::NUM_TILES) {
         if constexpr (CHAIN) {
-          if (!epilogue_tile<INT8, G2>(c, args, t - G1::NUM_TILES, a, st4, quad, cbase, lane, lead_tempty0, lead_tempty1)) break;
+          if (!epilogue_tile<INT8, G2>(c, args, t - G1::NUM_TILES, a, st4, quad, cbase, lane, lead_tempty0, lead_tempty1, ws,
+                                      rows_done)) break;
         }
       } else {
-        if (!epilogue_tile<INT8, G1>(c, args, t, a, st4, quad, cbase, lane, lead_tempty0, lead_tempty1)) break;
+        if (!epilogue_tile<INT8, G1>(c, args, t, a, st4, quad, cbase, lane, lead_tempty0, lead_tempty1, ws, rows_done)) break;
         if constexpr (CHAIN) ok = hand_over(c, args, ev++, lane);  // this warp's rows of the tile are stored
       }
     }
@@ -523,6 +599,16 @@ template <int M, int N, int K, bool INT8, bool A_MN, bool B_MN, class Epi>
 __device__ __forceinline__ void gemm_body_pair(const TgcbArgs& args, const TgcbTmaDesc* ta, const TgcbTmaDesc* tb) {
   using G = PairGemm<M, N, K, A_MN, B_MN, Epi>;
   pair_body<INT8, G, NoGemm, RoundRobin<G::NUM_TILES>>(args, ta, tb, ta, tb, nullptr);
+}
+
+// One GEMM on SM pairs with K cut into SPLIT slices (for GEMMs with fewer output tiles than
+// pairs): ws holds SPLIT x M x N partials, counters one zeroed word per 32 x 64 region of every
+// output tile (TILES x 32), both in the arena.
+template <int M, int N, int K, bool INT8, bool A_MN, bool B_MN, class Epi, int SPLIT>
+__device__ __forceinline__ void gemm_split_pair(const TgcbArgs& args, const TgcbTmaDesc* ta, const TgcbTmaDesc* tb,
+                                                void* ws, unsigned* counters) {
+  using G = PairGemm<M, N, K, A_MN, B_MN, Epi, SPLIT>;
+  pair_body<INT8, G, NoGemm, RoundRobin<G::NUM_TILES>>(args, ta, tb, ta, tb, counters, ws);
 }
 
 // Two GEMMs on SM pairs, the second reading the first's output as A, in one persistent launch.

@@ -237,10 +237,11 @@ int tgcb_plan_create(tgcb_module* m, const tgcb_launch_desc* launches, int n_lau
         return fail(TGCB_E_INVALID, "operand of %s lies outside the arena or the input table", ls.desc.kernel);
       }
     }
-    if (ls.desc.is_gemm == 3 && (ls.desc.counter_bytes == 0 || (ls.desc.counter_offset & 3u) != 0 ||
-                                 ls.desc.counter_offset + ls.desc.counter_bytes > arena_bytes)) {
+    if ((ls.desc.is_gemm == 3 && ls.desc.counter_bytes == 0) ||
+        (ls.desc.counter_bytes > 0 && (!ls.desc.is_gemm || (ls.desc.counter_offset & 3u) != 0 ||
+                                       ls.desc.counter_offset + ls.desc.counter_bytes > arena_bytes))) {
       delete p;
-      return fail(TGCB_E_INVALID, "the counters of chain %s lie outside the arena", ls.desc.kernel);
+      return fail(TGCB_E_INVALID, "the counters of %s lie outside the arena", ls.desc.kernel);
     }
   }
   *out = p;
@@ -345,6 +346,9 @@ int launch_one(DeviceState* st, LaunchState& ls, TgcbArgs& args, void* arena, co
                         clusters);
           ls.residency_checked = true;
         }
+      }
+      if (d.counter_bytes > 0) {
+        // a chain's row-block counters or a K split's region counters start at zero
         e = cudaMemsetAsync(static_cast<char*>(arena) + d.counter_offset, 0, d.counter_bytes, s);
         if (e != cudaSuccess) return fail(TGCB_E_CUDA, "zeroing the counters of %s: %s", d.kernel, cudaGetErrorString(e));
       }

@@ -51,6 +51,9 @@ ROW_PROLOGUE = True  # a one-warp-per-row step producing a chain's first A opera
 # training step's 65536 rows (28 rounds) kept the epilogue from its first accumulators and lost 0.8%
 ROW_PROLOGUE_MAX_ROUNDS = 4
 CHAIN_MAX_ITEMS = 32768  # tiles of both GEMMs together (the schedule is a __constant__ table)
+K_SPLIT = True  # an SM-pair GEMM with fewer output tiles than pairs cuts K into slices
+SPLIT_MAX = 8
+SPLIT_MIN_KBLOCKS = 16
 _LOAD_LINE = re.compile(r"^\s*const (.+?) (ld_\d+) = (.*);$")
 _LOAD_NAME = re.compile(r"\b(ld_\d+)\b")
 GEMM_THREADS = 576  # tgcb_gemm::THREADS: TMA warp, MMA warp, 16 epilogue warps
@@ -121,6 +124,7 @@ class PairGemmInfo:
     opb: GemmOperand
     epi_name: str
     epi_source: str
+    split_scratch: tuple[str, ...] = ()  # the K split's workspace and counters (dropped in a chain)
 
 
 @dataclass
@@ -572,7 +576,9 @@ class Lowering:
         how = (f"{first.bracketing} | then {second.bracketing} | both GEMMs in one launch: {len(items)} tiles on "
                f"{pairs} SM pairs in a fixed per-pair order, a tile of the second GEMM after its 256-row block of the first")
         reads = set(first.reads) | set(second.reads)
-        writes = list(first.writes) + [w for w in second.writes if w not in first.writes] + [counters]
+        unused = set(g1.split_scratch) | set(g2.split_scratch)
+        writes = [w for w in first.writes if w not in unused]
+        writes += [w for w in second.writes if w not in first.writes and w not in unused] + [counters]
         nodes = list(first.nodes) + list(second.nodes)
         if row is not None:
             how = (f"{row.bracketing}, the rows computed inside the launch by the epilogue warps (one warp per row) "
@@ -1113,21 +1119,37 @@ class Lowering:
             # Whole 256 x 256 tiles with the four-column epilogue run on SM pairs (two CTAs of a
             # cluster share one tcgen05.mma.cta_group::2 tile); everything else on single SMs.
             pair = vec4 is not None and M % 256 == 0 and N % 256 == 0 and PAIR_GEMM
+            split = self._k_split(M, N, K, is_int) if pair else 1
             body = "gemm_body_pair" if pair else "gemm_body"
-            kernel = (
-                f'extern "C" __global__ void __launch_bounds__({GEMM_THREADS}, 1) {kname}(const TgcbArgs args, '
-                "const __grid_constant__ TgcbTmaDesc ta, const __grid_constant__ TgcbTmaDesc tb) {\n"
-                f"  tgcb_gemm::{body}<{M}, {N}, {K}, {'true' if is_int else 'false'}, "
-                f"{'true' if opa.mn_major else 'false'}, {'true' if opb.mn_major else 'false'}, {epi_name}>(args, &ta, &tb);\n}}\n"
-            )
+            targs = (f"{M}, {N}, {K}, {'true' if is_int else 'false'}, {'true' if opa.mn_major else 'false'}, "
+                     f"{'true' if opb.mn_major else 'false'}, {epi_name}")
+            head = (f'extern "C" __global__ void __launch_bounds__({GEMM_THREADS}, 1) {kname}(const TgcbArgs args, '
+                    "const __grid_constant__ TgcbTmaDesc ta, const __grid_constant__ TgcbTmaDesc tb) {\n")
+            counters, counter_bytes = None, 0
+            if split > 1:
+                # K in `split` slices: partials in an arena workspace, one counter per 32 x 64
+                # region of every output tile (zeroed by the runtime before each launch)
+                ws, counters = f"{kname}_partials", f"{kname}_regions"
+                counter_bytes = (M // 256) * (N // 256) * 32 * 4
+                self.scratch[ws] = split * M * N * 4
+                self.scratch[counters] = counter_bytes
+                stores = stores + [ws, counters]
+                kernel = head + (f"  tgcb_gemm::gemm_split_pair<{targs}, {split}>(args, &ta, &tb, (void*)({PTR(ws)}), "
+                                 f"reinterpret_cast<unsigned*>({PTR(counters)}));\n}}\n")
+            else:
+                kernel = head + f"  tgcb_gemm::{body}<{targs}>(args, &ta, &tb);\n}}\n"
             if pair:
-                grid = 2 * max(1, min((M // 256) * (N // 256), NUM_SMS // 2))
+                grid = 2 * max(1, min((M // 256) * (N // 256) * split, NUM_SMS // 2))
             else:
                 grid = max(1, min(((M + 127) // 128) * ((N + 255) // 256), NUM_SMS))
-            launch = Launch(kname, (grid, 1, 1), (GEMM_THREADS, 1, 1), smem=-1, gemm=(opa, opb), pair=pair)
+            launch = Launch(kname, (grid, 1, 1), (GEMM_THREADS, 1, 1), smem=-1, gemm=(opa, opb), pair=pair,
+                            counters=counters, counter_bytes=counter_bytes)
             how = "tcgen05." + ("kind::i8, int32 accumulator in TMEM (exact)" if is_int else "kind::tf32, fp32 accumulator in TMEM, K in steps of 8")
             if pair:
                 how += "; SM pairs (cta_group::2), 256 x 256 tiles"
+            if split > 1:
+                how += (f"; K cut into {split} equal slices, each slice's partial stored, the slices of every "
+                        f"32 x 64 region summed in slice order by whichever slice finishes last")
         else:
             pair = False
             kernel = self._gemm_simt_kernel(kname, epi_name, M, N, K, is_int, a_base, a_flip, b_base, b_flip)
@@ -1142,8 +1164,28 @@ class Lowering:
             launches=[launch],
             bracketing=how,
             nodes=[name] + list(requests),
-            pair_gemm=PairGemmInfo(M, N, K, is_int, opa, opb, epi_name, epi) if pair else None,
+            # a chain, when this GEMM joins one, runs it unsplit (its tiles fill the other GEMM's waves)
+            pair_gemm=PairGemmInfo(M, N, K, is_int, opa, opb, epi_name, epi,
+                                   (counters, stores[-2]) if split > 1 else ()) if pair else None,
         )
+
+    def _k_split(self, M: int, N: int, K: int, is_int: bool) -> int:
+        """K slices for an SM-pair GEMM with at most half as many output tiles as SM pairs: the
+        most slices (up to SPLIT_MAX, at least SPLIT_MIN_KBLOCKS k-blocks each) whose items
+        all run at once. All slices then run side by side, so every slice's operands are read
+        from HBM once and shared through L2 by its tiles. With more items than pairs the
+        slices of one tile run in different rounds and re-read their operands: the training
+        step's weight gradients (64 tiles, 8 slices in 7 rounds) measured 3% slower split."""
+        pairs = NUM_SMS // 2
+        tiles = (M // 256) * (N // 256)
+        if not K_SPLIT or 2 * tiles > pairs:
+            return 1
+        kb = -(-K // (128 if is_int else 32))
+        best = 1
+        for s in range(2, SPLIT_MAX + 1):
+            if kb % s == 0 and kb // s >= SPLIT_MIN_KBLOCKS and tiles * s <= pairs:
+                best = s
+        return best
 
     def _gemm_vec4_epilogue(self, name: str, stores: list[str], M: int, N: int, acc_t: str,
                             whole_tiles: bool = False) -> str | None:

@@ -238,6 +238,8 @@ def generate(graph, *, pipeline=None, optimise: bool = True) -> tuple:
                 if ln.gemm2 is not None:
                     d.a2 = _operand_desc(ln.gemm2[0], lowering, offsets, 128)
                     d.b2 = _operand_desc(ln.gemm2[1], lowering, offsets, 128)
+                if ln.counters is not None:
+                    # a chain's row-block counters or a K split's region counters
                     d.counter_offset = offsets[ln.counters]
                     d.counter_bytes = ln.counter_bytes
             else:
