@@ -83,3 +83,48 @@ def test_no_chain_when_disabled(monkeypatch):
     monkeypatch.setattr(codegen, "CHAIN_GEMM", False)
     mod = runtime.generate(workloads.mlp_graph(ir.Builder))[3]
     assert [s.kind for s in mod.steps] == ["row", "gemm", "gemm"]
+
+
+def test_layernorm_becomes_the_chains_row_prologue_only_for_few_rows():
+    # 8192 rows: 512 groups of 16 rows, 4 per CTA -> inside the chain launch
+    mod = runtime.generate(workloads.mlp_graph(ir.Builder, rows=8192))[3]
+    assert [s.kind for s in mod.steps] == ["gemm"]
+    assert "Rows_" in mod.steps[0].source
+    # 65536 rows: 28 groups per CTA would hold the epilogue warps back -> its own launch
+    mod = runtime.generate(workloads.mlp_graph(ir.Builder, rows=65536))[3]
+    assert [s.kind for s in mod.steps] == ["row", "gemm"]
+    # 64 threads per row (2048 rows of 1024): shared-memory partials, never a prologue
+    mod = runtime.generate(workloads.mlp_graph(ir.Builder, rows=2048))[3]
+    assert [s.kind for s in mod.steps] == ["row", "gemm"]
+
+
+@pytest.mark.parametrize(
+    "m,n,k,split",
+    [
+        (1024, 1024, 65536, 4),   # 16 tiles: 4 slices fill 64 of 74 pairs
+        (512, 1024, 65536, 8),    # 8 tiles
+        (256, 256, 4096, 8),      # 1 tile, 128 k-blocks: 8 slices of 16
+        (256, 256, 1024, 2),      # 32 k-blocks: 2 slices of 16
+        (256, 256, 256, 1),       # 8 k-blocks: too short to split
+        (1024, 4096, 65536, 1),   # 64 tiles: slices would run in different rounds
+        (2048, 2048, 65536, 1),   # 64 tiles
+    ],
+)
+def test_k_split_only_when_every_slice_runs_at_once(m, n, k, split):
+    b = ir.Builder()
+    x = b.input((k, m), ir.FLOAT32, "x")
+    dy = b.input((k, n), ir.FLOAT32, "dy")
+    mod = runtime.generate(b.finish(b.matmul(b.transpose(x, [1, 0]), dy)))[3]
+    (step,) = mod.steps
+    (launch,) = step.launches
+    tiles = (m // 256) * (n // 256)
+    if split == 1:
+        assert launch.counters is None and "slices" not in step.bracketing
+        return
+    assert f"K cut into {split} equal slices" in step.bracketing
+    assert f"gemm_split_pair<{m}, {n}, {k}, false, true, true, Epi_tgcb_gemm_1, {split}>" in step.source
+    assert launch.grid[0] == 2 * tiles * split and tiles * split <= codegen.NUM_SMS // 2
+    assert launch.counter_bytes == tiles * 32 * 4
+    # the workspace holds every slice's partial
+    ws = [w for w in step.writes if w.endswith("_partials")]
+    assert len(ws) == 1 and mod.offsets[ws[0]] % 256 == 0
