@@ -1115,6 +1115,7 @@ class Lowering:
         )
         reads = {a_base, b_base}  # plus whatever the epilogue loads (recorded by _pointer_of)
         tma_ok = all((op.cols * op.elem_bytes) % 16 == 0 for op in (opa, opb))
+        split_scratch: tuple[str, ...] = ()  # a K split's workspace and counters
         if tma_ok:
             # Whole 256 x 256 tiles with the four-column epilogue run on SM pairs (two CTAs of a
             # cluster share one tcgen05.mma.cta_group::2 tile); everything else on single SMs.
@@ -1133,7 +1134,8 @@ class Lowering:
                 counter_bytes = (M // 256) * (N // 256) * 32 * 4
                 self.scratch[ws] = split * M * N * 4
                 self.scratch[counters] = counter_bytes
-                stores = stores + [ws, counters]
+                split_scratch = (ws, counters)
+                stores = stores + list(split_scratch)
                 kernel = head + (f"  tgcb_gemm::gemm_split_pair<{targs}, {split}>(args, &ta, &tb, (void*)({PTR(ws)}), "
                                  f"reinterpret_cast<unsigned*>({PTR(counters)}));\n}}\n")
             else:
@@ -1165,8 +1167,7 @@ class Lowering:
             bracketing=how,
             nodes=[name] + list(requests),
             # a chain, when this GEMM joins one, runs it unsplit (its tiles fill the other GEMM's waves)
-            pair_gemm=PairGemmInfo(M, N, K, is_int, opa, opb, epi_name, epi,
-                                   (counters, stores[-2]) if split > 1 else ()) if pair else None,
+            pair_gemm=PairGemmInfo(M, N, K, is_int, opa, opb, epi_name, epi, split_scratch) if pair else None,
         )
 
     def _k_split(self, M: int, N: int, K: int, is_int: bool) -> int:
