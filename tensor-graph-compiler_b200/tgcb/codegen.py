@@ -159,6 +159,9 @@ def row_threads(cols: int, rows: int | None = None) -> int:
 
 
 ROW_BLOCK = 256  # threads per CTA of a row kernel; 256 // T rows are processed side by side
+# a standalone row kernel issues all of its first phase's loads before any arithmetic, so each
+# thread has its whole row slice in flight at once (the order of the additions is unchanged)
+ROW_HOIST_LOADS = True
 
 
 class Lowering:
@@ -734,6 +737,7 @@ class Lowering:
         row_req = [r for r in requests if self.sizes(r) != ss]
         reads: set[str] = set()
         lines: list[str] = []
+        hoisted: list[str] = []  # the standalone kernel's lines, first-phase loads moved up
         nred = len(members)
         slot = {m: k for k, m in enumerate(members)}
 
@@ -767,6 +771,7 @@ class Lowering:
                 eb = ExprBuilder(self.values, self.producers, self._pointer_of, member_resolve, indent="      ")
                 ks = [0]
                 lines.append(f"    for (long long col = tid; col < {C}LL; col += {T}LL) {{")
+            phase_start = len(lines)
             for k in ks:
                 col = col_expr(k)
                 colc = f"tgcb_min_ll({col}, {C - 1}LL)" if (unrolled and C % T) else col
@@ -783,6 +788,13 @@ class Lowering:
                 if unrolled:
                     lines.extend(eb.lines)
                     eb.lines = []
+            if unrolled and phase == 1:
+                # load offsets are index arithmetic on tid, row and constants only, so every
+                # load of the phase can move ahead of the phase's arithmetic
+                body = lines[phase_start:]
+                hoisted = lines[:phase_start] + [ln for ln in body if _LOAD_LINE.match(ln)] + [
+                    ln for ln in body if not _LOAD_LINE.match(ln)
+                ]
             if not unrolled:
                 lines.extend(eb.lines)
                 lines.append("    }")
@@ -831,6 +843,7 @@ class Lowering:
         reads |= shared_eb.loads
         row_blocks = (R + RPB - 1) // RPB
         grid = max(1, min(row_blocks, NUM_SMS * (2048 // ROW_BLOCK) * 2))
+        kernel_lines = hoisted + lines[len(hoisted):] if (hoisted and ROW_HOIST_LOADS) else lines
         src = (
             f'extern "C" __global__ void __launch_bounds__({ROW_BLOCK}) {kname}(const TgcbArgs args) {{\n'
             f"  __shared__ double red_smem[{nred}][{RPB}][{W}];\n"
@@ -839,7 +852,7 @@ class Lowering:
             f"  for (long long rb = (long long)blockIdx.x * {RPB}; rb < {R}LL; rb += (long long)gridDim.x * {RPB}) {{\n"
             f"    const bool live = rb + grp < {R}LL;\n"
             f"    const long long row = live ? rb + grp : {R - 1}LL;\n"
-            + "\n".join(lines)
+            + "\n".join(kernel_lines)
             + "\n  }\n}\n"
         )
         writes = [m for m in members if m in self.materialised] + list(requests)
