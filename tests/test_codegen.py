@@ -30,6 +30,31 @@ def test_cone_is_one_row_kernel():
     assert set(mod.steps[0].writes) == set(low.outputs)
 
 
+def test_row_kernel_issues_its_loads_before_the_arithmetic(monkeypatch):
+    """The cone's thread loads its 16 columns first; the additions keep their column order."""
+    (step,) = runtime.generate(workloads.cone_graph(ir.Builder))[3].steps
+    body = step.source[step.source.index("float acc_2"):]
+    loads = [i for i, ln in enumerate(body.splitlines()) if "__ldg(" in ln]
+    first_exp = next(i for i, ln in enumerate(body.splitlines()) if "expf(" in ln)
+    assert len(loads) == 16 and max(loads) < first_exp
+    offsets = [f"(long long)tid + {64 * k}LL" for k in range(16)]
+    assert [body.index(o) for o in offsets] == sorted(body.index(o) for o in offsets)
+    monkeypatch.setattr(codegen, "ROW_HOIST_LOADS", False)
+    (inline,) = runtime.generate(workloads.cone_graph(ir.Builder))[3].steps
+    lines = inline.source.splitlines()
+    assert sorted(lines) == sorted(step.source.splitlines())  # the same statements, reordered
+    assert lines != step.source.splitlines()
+
+
+def test_row_prologue_body_keeps_loads_inline():
+    """Inside the GEMM chain the layernorm body is left in its inline order (register budget)."""
+    _, _, _, mod, _ = runtime.generate(workloads.mlp_graph(ir.Builder))
+    src = mod.steps[0].source
+    body = src[src.index("struct Rows_"):]
+    first_add = body.index("acc_0 = acc_0 +")
+    assert body.index("__ldg(") < first_add < body.rindex("__ldg(")
+
+
 def test_mlp_is_layernorm_then_two_gemms(monkeypatch):
     monkeypatch.setattr(codegen, "CHAIN_GEMM", False)
     _, _, plan, mod, low = runtime.generate(workloads.mlp_graph(ir.Builder))
