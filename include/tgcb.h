@@ -113,6 +113,14 @@ int tgcb_plan_create(tgcb_module* m, const tgcb_launch_desc* launches, int n_lau
                      tgcb_plan** out);
 void tgcb_plan_destroy(tgcb_plan* p);
 
+/* Declare that the plan's kernels read graph inputs 0 .. n_inputs-1 (the generated code indexes
+ * them without checks). Every later run of the plan then refuses, with TGCB_E_INVALID and
+ * before queueing anything, an input table shorter than n_inputs or one holding a null pointer
+ * among them, instead of letting a kernel read through it. A plan whose count was never set
+ * (0) checks nothing. The C-side counterpart of the refusal of a call that lacks a feed in
+ * CompiledGraph.__call__ (tgc/runtime/executor.py:74-78). */
+int tgcb_plan_set_input_count(tgcb_plan* p, int n_inputs);
+
 /* Launch every kernel of the plan in order on `stream`. `arena` is a device allocation of at
  * least arena_bytes (256-byte aligned); inputs[i] is the device address of graph input i
  * (read only). Asynchronous: returns after the launches are queued.

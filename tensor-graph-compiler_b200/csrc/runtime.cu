@@ -94,6 +94,7 @@ struct LaunchState {
 struct tgcb_plan {
   std::vector<LaunchState> launches;
   uint64_t arena_bytes = 0;
+  int input_count = 0;  // graph inputs the kernels read (tgcb_plan_set_input_count); 0: unchecked
 };
 
 extern "C" {
@@ -250,6 +251,14 @@ int tgcb_plan_create(tgcb_module* m, const tgcb_launch_desc* launches, int n_lau
 
 void tgcb_plan_destroy(tgcb_plan* p) { delete p; }
 
+int tgcb_plan_set_input_count(tgcb_plan* p, int n_inputs) {
+  if (p == nullptr) return fail(TGCB_E_INVALID, "tgcb_plan_set_input_count: null plan");
+  if (n_inputs < 0 || n_inputs > TGCB_MAX_INPUTS)
+    return fail(TGCB_E_INVALID, "a plan reads 0 to %d inputs, not %d", TGCB_MAX_INPUTS, n_inputs);
+  p->input_count = n_inputs;
+  return TGCB_OK;
+}
+
 int tgcb_plan_launch_count(const tgcb_plan* p) { return p ? (int)p->launches.size() : 0; }
 
 static int encode_operand(DeviceState* st, const tgcb_operand_desc& od, const void* base, CUtensorMap* map) {
@@ -280,6 +289,11 @@ int prepare_run(tgcb_plan* p, void* arena, const void* const* inputs, int n_inpu
   if (p == nullptr) return fail(TGCB_E_INVALID, "tgcb_plan_run: null plan");
   if (n_inputs < 0 || n_inputs > TGCB_MAX_INPUTS)
     return fail(TGCB_E_INVALID, "a plan takes at most %d inputs, got %d", TGCB_MAX_INPUTS, n_inputs);
+  if (n_inputs > 0 && inputs == nullptr) return fail(TGCB_E_INVALID, "tgcb_plan_run: null input table");
+  if (n_inputs < p->input_count)
+    return fail(TGCB_E_INVALID, "the plan reads %d inputs, the run passes %d", p->input_count, n_inputs);
+  for (int i = 0; i < p->input_count; ++i)
+    if (inputs[i] == nullptr) return fail(TGCB_E_INVALID, "input %d of the run is a null pointer", i);
   if (p->arena_bytes > 0 && arena == nullptr) return fail(TGCB_E_INVALID, "tgcb_plan_run: null arena");
   if ((reinterpret_cast<uintptr_t>(arena) & 255u) != 0) return fail(TGCB_E_INVALID, "the arena is not 256-byte aligned");
   int rc = current_state(st);

@@ -82,6 +82,7 @@ SIGNATURES = {
         [ctypes.c_void_p, ctypes.POINTER(LaunchDesc), ctypes.c_int, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)],
     ),
     "tgcb_plan_destroy": (None, [ctypes.c_void_p]),
+    "tgcb_plan_set_input_count": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "tgcb_plan_run": (
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_void_p],

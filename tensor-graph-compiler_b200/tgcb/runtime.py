@@ -294,6 +294,7 @@ class CompiledGraph:
                 "binding the launch plan",
             )
             self._plan = plan_h
+            _lib.check(lib.tgcb_plan_set_input_count(plan_h, len(self.input_names)), "declaring the plan's inputs")
         self._out_specs = []
         for name in module.output_names:
             v = lowering.values[name]

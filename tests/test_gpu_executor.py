@@ -9,6 +9,7 @@ torch on the CPU; here the arithmetic is the GPU's)."""
 
 from __future__ import annotations
 
+import ctypes
 import os
 
 import pytest
@@ -16,8 +17,8 @@ import torch
 from conftest import GOLDEN
 
 from oracle import interp
-from tgcb import serialize
-from tgcb.errors import ConfigError
+from tgcb import _lib, serialize
+from tgcb.errors import AllocationError, ConfigError
 from tgcb.runtime import compile_graph
 
 pytestmark = pytest.mark.gpu
@@ -74,3 +75,29 @@ def test_a_missing_input_is_reported(cuda):
     compiled = compile_graph(load("softmax"))
     with pytest.raises(ConfigError, match="no value supplied"):
         compiled({})
+
+
+def test_a_short_or_null_input_table_is_refused_before_any_launch(cuda):
+    """A C caller of tgcb_plan_run gets TGCB_E_INVALID, not a kernel reading through a null
+    pointer, when its input table is short or holds a null entry; the plan still runs after."""
+    graph = load("mlp")
+    compiled = compile_graph(graph)
+    assert len(compiled.input_names) > 1
+    feeds = interp.random_feeds(graph, seed=0, positive=True)
+    arena = compiled.new_arena()
+    ptrs = compiled.input_pointers(arena, {n: t.to(cuda) for n, t in feeds.items()})
+    torch.cuda.synchronize()
+    lib = _lib.load()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    short = (ctypes.c_void_p * len(ptrs))(*ptrs)
+    rc = lib.tgcb_plan_run(compiled._plan, ctypes.c_void_p(arena.data_ptr()), short, len(ptrs) - 1, stream)
+    assert rc == _lib.TGCB_E_INVALID and "the plan reads" in _lib.last_error()
+    holed = (ctypes.c_void_p * len(ptrs))(*ptrs)
+    holed[len(ptrs) - 1] = None
+    rc = lib.tgcb_plan_run(compiled._plan, ctypes.c_void_p(arena.data_ptr()), holed, len(ptrs), stream)
+    assert rc == _lib.TGCB_E_INVALID and "null pointer" in _lib.last_error()
+    with pytest.raises(AllocationError, match="the plan reads"):
+        _lib.check(lib.tgcb_plan_run(compiled._plan, ctypes.c_void_p(arena.data_ptr()), short, 0, stream), "run")
+    compiled.check_status()  # nothing was launched by the refused calls
+    got = compiled.function(arena, {n: t.to(cuda) for n, t in feeds.items()})
+    assert agree(got, interp.run(graph, feeds), gemm=True)

@@ -42,6 +42,7 @@ def test_argument_errors_need_no_gpu():
     assert lib.tgcb_sum_pairwise_f32(None, 10, 8, None, None, 0, None) == _lib.TGCB_E_INVALID
     assert "null" in _lib.last_error()
     assert lib.tgcb_plan_run(None, None, None, 0, None) == _lib.TGCB_E_INVALID
+    assert lib.tgcb_plan_set_input_count(None, 1) == _lib.TGCB_E_INVALID
     assert lib.tgcb_quantise_rows_i8(None, 0, 0, None, None, None) == _lib.TGCB_E_INVALID
     assert lib.tgcb_sum_pairwise_scratch_bytes(1 << 26, 8) > 0
 
