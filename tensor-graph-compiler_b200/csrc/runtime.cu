@@ -57,6 +57,16 @@ struct DeviceState {
 DeviceState g_devices[kMaxDevices];
 std::mutex g_mutex;
 
+// offset + rows * cols * elem_bytes <= limit, without wrapping around on absurd descriptors
+bool fits(uint64_t offset, uint64_t rows, uint64_t cols, uint64_t elem_bytes, uint64_t limit) {
+  if (offset > limit) return false;
+  const uint64_t room = limit - offset;
+  if (elem_bytes == 0 || rows == 0 || cols == 0) return true;
+  if (cols > room / elem_bytes) return false;
+  const uint64_t row_bytes = cols * elem_bytes;
+  return rows <= room / row_bytes;
+}
+
 int current_state(DeviceState** out) {
   int dev = 0;
   CUDA_TRY(cudaGetDevice(&dev));
@@ -120,7 +130,7 @@ int tgcb_init(int device) {
   CUDA_TRY(cudaSetDevice(device));
   DeviceState& st = g_devices[device];
   if (st.ready) return TGCB_OK;
-  CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&st.status), 256));
+  if (st.status == nullptr) CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&st.status), 256));  // kept if a later step fails
   CUDA_TRY(cudaMemset(st.status, 0, 256));
   void* fn = nullptr;
   cudaDriverEntryPointQueryResult q;
@@ -231,16 +241,15 @@ int tgcb_plan_create(tgcb_module* m, const tgcb_launch_desc* launches, int n_lau
     const tgcb_operand_desc* ops[4] = {&ls.desc.a, &ls.desc.b, &ls.desc.a2, &ls.desc.b2};
     for (int k = 0; k < n_ops; ++k) {
       const tgcb_operand_desc* od = ops[k];
-      if (od->input_index >= TGCB_MAX_INPUTS || (od->input_index < 0 && od->arena_offset + od->rows * od->cols *
-                                                                                                 od->elem_bytes >
-                                                                             arena_bytes)) {
+      if (od->input_index >= TGCB_MAX_INPUTS || (od->input_index < 0 && !fits(od->arena_offset, od->rows, od->cols,
+                                                                               od->elem_bytes, arena_bytes))) {
         delete p;
         return fail(TGCB_E_INVALID, "operand of %s lies outside the arena or the input table", ls.desc.kernel);
       }
     }
     if ((ls.desc.is_gemm == 3 && ls.desc.counter_bytes == 0) ||
         (ls.desc.counter_bytes > 0 && (!ls.desc.is_gemm || (ls.desc.counter_offset & 3u) != 0 ||
-                                       ls.desc.counter_offset + ls.desc.counter_bytes > arena_bytes))) {
+                                       !fits(ls.desc.counter_offset, 1, ls.desc.counter_bytes, 1, arena_bytes)))) {
       delete p;
       return fail(TGCB_E_INVALID, "the counters of %s lie outside the arena", ls.desc.kernel);
     }

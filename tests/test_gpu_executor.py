@@ -101,3 +101,41 @@ def test_a_short_or_null_input_table_is_refused_before_any_launch(cuda):
     compiled.check_status()  # nothing was launched by the refused calls
     got = compiled.function(arena, {n: t.to(cuda) for n, t in feeds.items()})
     assert agree(got, interp.run(graph, feeds), gemm=True)
+
+
+def test_descriptors_outside_the_arena_are_refused(cuda):
+    """tgcb_plan_create checks every GEMM operand and counter range against the arena, also for
+    sizes whose byte count would wrap around 64 bits; nothing is launched."""
+    compiled = compile_graph(load("mlp"))
+    lib = _lib.load()
+    gemm = next(d for d in compiled.module.launches if d.is_gemm)
+
+    def create(edit) -> int:
+        d = _lib.LaunchDesc()
+        ctypes.pointer(d)[0] = gemm
+        edit(d)
+        plan = ctypes.c_void_p()
+        rc = lib.tgcb_plan_create(compiled._module, (_lib.LaunchDesc * 1)(d), 1, compiled.arena_bytes, ctypes.byref(plan))
+        if rc == _lib.TGCB_OK:
+            lib.tgcb_plan_destroy(plan)
+        return rc
+
+    def arena_operand(offset, rows, cols):
+        def edit(d):
+            d.a.input_index, d.a.arena_offset, d.a.rows, d.a.cols = -1, offset, rows, cols
+        return edit
+
+    assert create(lambda d: None) == _lib.TGCB_OK
+    assert create(arena_operand(compiled.arena_bytes, 1, 1)) == _lib.TGCB_E_INVALID
+    assert "outside the arena" in _lib.last_error()
+    assert create(arena_operand(0, 1 << 40, 1 << 40)) == _lib.TGCB_E_INVALID  # 2^80 * 4 bytes wraps
+    assert create(arena_operand((1 << 64) - 16, 1, 8)) == _lib.TGCB_E_INVALID  # offset + size wraps
+
+    def counters(offset, nbytes):
+        def edit(d):
+            d.counter_offset, d.counter_bytes = offset, nbytes
+        return edit
+
+    assert create(counters((1 << 64) - 4, 8)) == _lib.TGCB_E_INVALID
+    assert create(counters(0, compiled.arena_bytes + 4)) == _lib.TGCB_E_INVALID
+    assert create(counters(0, 256)) == _lib.TGCB_OK
