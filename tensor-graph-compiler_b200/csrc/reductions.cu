@@ -342,53 +342,74 @@ __global__ void __launch_bounds__(256) quantise_rows(const float* __restrict__ x
 // holding V float4 of its row in registers (columns 4(t + 256k) .. +3). max|x| is exact in any
 // order and the quantisation is elementwise, so this layout changes no result; it only makes
 // every load 16 bytes and every store 4 bytes wide.
+//
+// max|x| is the unsigned maximum of the sign-cleared bit patterns: for non-negative floats the
+// unsigned order is the numeric order and every NaN pattern lies above +inf, so a NaN anywhere
+// in the row gives a NaN maximum (and every element of that row takes the exact quotient).
+//
+// rint(x / s) without a division per element: t = x * (1/s) with the correctly rounded
+// reciprocal differs from the correctly rounded quotient by at most 2 * 2^-24 * |x/s| (two
+// roundings), below 1.6e-5 for |x/s| <= 128 (|x| <= m here). Unless t lies within 3e-5 of a
+// half-integer, both round to the same integer; near a half-integer the exact quotient
+// decides. t - rint(t) is exact for |t| <= 128 (Sterbenz). When m and 1/s are finite (uniform
+// over the row) every |x / s| is at most 127 * (1 + 2^-21) even for a subnormal s, so the
+// rounded value lies in [-127, 127] and needs no clamp; rows with a non-finite m or 1/s take
+// the exact quotient with the clamp to [-128, 127] for every element.
 template <int V>
-__global__ void __launch_bounds__(256) quantise_rows_vec(const float* __restrict__ x, long long cols, int8_t* __restrict__ q,
-                                                         float* __restrict__ scale) {
-  __shared__ float red[8];
+__global__ void __launch_bounds__(256) quantise_rows_vec(const float* __restrict__ x, long long cols,
+                                                          int8_t* __restrict__ q, float* __restrict__ scale) {
+  __shared__ unsigned red[8];
   const long long r = blockIdx.x;
   const float4* row = reinterpret_cast<const float4*>(x + r * cols);
   float4 v[V];
-  float m = 0.0f;
+#pragma unroll
+  for (int k = 0; k < V; ++k) v[k] = __ldg(row + threadIdx.x + 256 * k);
+  unsigned m = 0u;
 #pragma unroll
   for (int k = 0; k < V; ++k) {
-    v[k] = __ldg(row + threadIdx.x + 256 * k);
-    const float a[4] = {fabsf(v[k].x), fabsf(v[k].y), fabsf(v[k].z), fabsf(v[k].w)};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) m = (a[i] > m || a[i] != a[i]) ? a[i] : m;
+    m = max(m, __float_as_uint(v[k].x) & 0x7fffffffu);
+    m = max(m, __float_as_uint(v[k].y) & 0x7fffffffu);
+    m = max(m, __float_as_uint(v[k].z) & 0x7fffffffu);
+    m = max(m, __float_as_uint(v[k].w) & 0x7fffffffu);
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float other = __shfl_xor_sync(0xffffffffu, m, o);
-    m = (other > m || other != other) ? other : m;
-  }
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
-  float mm = red[0];
+  unsigned mb = red[0];
 #pragma unroll
-  for (int w = 1; w < 8; ++w) mm = (red[w] > mm || red[w] != red[w]) ? red[w] : mm;
+  for (int w = 1; w < 8; ++w) mb = max(mb, red[w]);
+  const float mm = __uint_as_float(mb);
   const float s = (mm == 0.0f) ? 1.0f : (float)((double)mm / 127.0);
   if (threadIdx.x == 0) scale[r] = s;
-  // rint(x / s) without a division per element: t = x * (1/s) with the correctly rounded
-  // reciprocal differs from the correctly rounded quotient by at most 1.5 * 2^-23 * |x/s|,
-  // which is below 2.3e-5 for |x/s| <= 128 (|x| <= m here). Unless t lies within 3e-5 of a
-  // half-integer, both round to the same integer; near a half-integer (or for non-finite
-  // values) the exact quotient decides. t - rint(t) is exact for |t| <= 128 (Sterbenz).
   const float inv = __fdiv_rn(1.0f, s);
-  const bool fast = isfinite(inv) && isfinite(mm);
   char4* qrow = reinterpret_cast<char4*>(q + r * cols);
+  if (isfinite(inv) && isfinite(mm)) {
 #pragma unroll
-  for (int k = 0; k < V; ++k) {
-    const float e[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-    signed char b[4];
+    for (int k = 0; k < V; ++k) {
+      const float e[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+      signed char b[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float t = e[i] * inv;
-      float qi = rintf(t);
-      if (!fast || fabsf(0.5f - fabsf(t - qi)) <= 3e-5f) qi = rintf(__fdiv_rn(e[i], s));
-      b[i] = (signed char)(int)fminf(fmaxf(qi, -128.0f), 127.0f);
+      for (int i = 0; i < 4; ++i) {
+        const float t = e[i] * inv;
+        float qi = rintf(t);
+        if (fabsf(0.5f - fabsf(t - qi)) <= 3e-5f) qi = rintf(__fdiv_rn(e[i], s));
+        b[i] = (signed char)(int)qi;
+      }
+      qrow[threadIdx.x + 256 * k] = make_char4(b[0], b[1], b[2], b[3]);
     }
-    qrow[threadIdx.x + 256 * k] = make_char4(b[0], b[1], b[2], b[3]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const float e[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+      signed char b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float qi = rintf(__fdiv_rn(e[i], s));
+        b[i] = (signed char)(int)fminf(fmaxf(qi, -128.0f), 127.0f);
+      }
+      qrow[threadIdx.x + 256 * k] = make_char4(b[0], b[1], b[2], b[3]);
+    }
   }
 }
 
