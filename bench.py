@@ -809,15 +809,25 @@ def cpu_baseline(wl, budget_s: float) -> dict:
 
 
 def read_traffic(workload: str, kernel: str):
-    """DRAM bytes per launch of the dominant kernel, from the committed ncu summary (by kernel name)."""
+    """DRAM bytes per launch of the dominant kernel, from the committed ncu summary.
+
+    Lines read ``workload kernel-name bytes  # note``; a kernel name may hold spaces. A dominant
+    "kernel" named ``a+b`` (a launch and the dependent launch that finishes it) gets the sum of
+    its parts when every part is listed, else None."""
     path = os.path.join(REPO, "profiles", "ncu_traffic.txt")
     if not os.path.exists(path):
         return None
+    table = {}
     with open(path) as f:
         for line in f:
-            parts = line.split()
-            if len(parts) >= 3 and not line.startswith("#") and parts[0] == workload and parts[1] == kernel:
-                return int(parts[2])
+            if line.startswith("#"):
+                continue
+            parts = line.split("#", 1)[0].split()
+            if len(parts) >= 3 and parts[-1].isdigit():
+                table[(parts[0], " ".join(parts[1:-1]))] = int(parts[-1])
+    names = kernel.split("+")
+    if all((workload, n) in table for n in names):
+        return sum(table[(workload, n)] for n in names)
     return None
 
 

@@ -200,6 +200,37 @@ __device__ __forceinline__ float chunk_tree(const float* p) {
   return v[0];
 }
 
+// chunk_tree's values for C in 4..32 when the partials are 16-byte aligned. Loading thread t's
+// C consecutive partials per thread makes every warp load touch 32 cache lines; instead the
+// block loads all 256 * C partials with coalesced 16-byte loads into shared-memory rows of
+// C + 1 words (one row per thread: an odd row pitch puts the 32 rows a warp reads on 32
+// different banks), then each thread adds its row as the same perfect tree.
+constexpr int kStageRow = 33;  // words per staged row: C + 1 for the widest C, 32
+template <int C>
+__device__ __forceinline__ float staged_chunk_tree(const float* p, float* stage) {
+  static_assert(C % 4 == 0 && C <= kStageRow - 1, "a float4 must stay inside one row");
+  const float4* p4 = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int k = 0; k < C / 4; ++k) {
+    const int j = threadIdx.x + kGroup * k;  // float4 index into the block's 256 * C partials
+    const float4 q = __ldcg(p4 + j);
+    float* d = stage + (4 * j / C) * (C + 1) + (4 * j) % C;
+    d[0] = q.x;
+    d[1] = q.y;
+    d[2] = q.z;
+    d[3] = q.w;
+  }
+  __syncthreads();
+  float v[C];
+#pragma unroll
+  for (int i = 0; i < C; ++i) v[i] = stage[threadIdx.x * (C + 1) + i];
+#pragma unroll
+  for (int w = 1; w < C; w *= 2)
+#pragma unroll
+    for (int i = 0; i < C; i += 2 * w) v[i] = __fadd_rn(v[i], v[i + w]);
+  return v[0];
+}
+
 // The two launches of a wide uniform sum. The leaf kernel lets its dependent launch start at
 // once (programmatic dependent launch), so the final kernel is resident and waiting when the
 // last leaf block retires, instead of paying a launch gap. The final kernel (one block) waits
@@ -213,9 +244,23 @@ __global__ void __launch_bounds__(kGroup) pairwise_leaves_pdl(const float* __res
   if (threadIdx.x == 0) out[blockIdx.x] = r;
 }
 
-__global__ void __launch_bounds__(kGroup) pairwise_final(const float* partials, int per, float* __restrict__ out) {
+__global__ void __launch_bounds__(kGroup) pairwise_final(const float* partials, int per, int staged,
+                                                          float* __restrict__ out) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ float s[kGroup / 32];
+  __shared__ float stage[kGroup * kStageRow];
+  if (staged) {  // the host sets it only for per in {4, 8, 16, 32} and 16-byte aligned partials
+    float v;
+    switch (per) {
+      case 4: v = staged_chunk_tree<4>(partials, stage); break;
+      case 8: v = staged_chunk_tree<8>(partials, stage); break;
+      case 16: v = staged_chunk_tree<16>(partials, stage); break;
+      default: v = staged_chunk_tree<32>(partials, stage); break;
+    }
+    const float t = fast_block_tree(v, s);
+    if (threadIdx.x == 0) out[0] = t;
+    return;
+  }
   const float* p = partials + (long long)threadIdx.x * per;
   float v;
   switch (per) {
@@ -467,7 +512,9 @@ int tgcb_sum_pairwise_f32(const float* x, uint64_t n, int block, float* out, voi
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, pairwise_final, (const float*)buf, (int)(grid / kGroup), out);
+    const int per = (int)(grid / kGroup);
+    const int staged = per >= 4 && per <= 32 && (reinterpret_cast<uintptr_t>(buf) & 15u) == 0;
+    e = cudaLaunchKernelEx(&cfg, pairwise_final, (const float*)buf, per, staged, out);
     if (e != cudaSuccess) return report(TGCB_E_CUDA, "pairwise_final", e);
     return TGCB_OK;
   }
