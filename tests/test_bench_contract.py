@@ -40,3 +40,22 @@ def test_gpu_arm_gives_no_number_without_a_gpu():
     p = _run("--steps", "1", "--warmup", "1", "--no-cpu-baseline", timeout=300)
     assert p.returncode != 0
     assert not [ln for ln in p.stdout.splitlines() if ln.strip().startswith("{")]
+
+
+def test_traffic_lines_parse(tmp_path, monkeypatch):
+    """profiles/ncu_traffic.txt: names may hold spaces; a composite "a+b" sums its listed parts."""
+    sys.path.insert(0, REPO)
+    import bench
+
+    (tmp_path / "profiles").mkdir()
+    (tmp_path / "profiles" / "ncu_traffic.txt").write_text(
+        "# workload kernel bytes\n"
+        "w void k<4> 100  # a note\n"
+        "w leaf 200\n"
+        "w final 5\n"
+    )
+    monkeypatch.setattr(bench, "REPO", str(tmp_path))
+    assert bench.read_traffic("w", "void k<4>") == 100
+    assert bench.read_traffic("w", "leaf+final") == 205
+    assert bench.read_traffic("w", "leaf+missing") is None
+    assert bench.read_traffic("other", "leaf") is None
