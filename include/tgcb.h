@@ -105,6 +105,8 @@ void tgcb_free(void* p);
 
 /* Load a cubin produced by tgcb_compile_cubin into the current context. */
 int tgcb_module_load(const void* cubin, size_t size, tgcb_module** out);
+/* Waits for the current device (its kernels may still be running), then releases the module.
+ * Call it with the device the module's plans ran on current; destroy those plans first. */
 void tgcb_module_unload(tgcb_module* m);
 
 /* Resolve each launch's kernel in `m` and keep the descriptors.

@@ -204,6 +204,10 @@ int tgcb_module_load(const void* cubin, size_t size, tgcb_module** out) {
 
 void tgcb_module_unload(tgcb_module* m) {
   if (m == nullptr) return;
+  // kernels of this module queued on the current device may still be running: let them finish
+  // before their code is released
+  cudaDeviceSynchronize();
+  cudaGetLastError();
   if (m->lib) cudaLibraryUnload(m->lib);
   delete m;
 }

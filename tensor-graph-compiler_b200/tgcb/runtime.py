@@ -312,7 +312,9 @@ class CompiledGraph:
             if getattr(self, "_plan", None):
                 lib.tgcb_plan_destroy(self._plan)
             if getattr(self, "_module", None):
-                lib.tgcb_module_unload(self._module)
+                # the unload waits for this device: the last call's kernels may still be running
+                with self._torch.cuda.device(self.device):
+                    lib.tgcb_module_unload(self._module)
         except Exception:  # noqa: BLE001 - interpreter shutdown
             pass
 
