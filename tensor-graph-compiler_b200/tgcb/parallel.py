@@ -9,8 +9,11 @@ one GPU; it compiles the gradient graph of its own shard (``tgcb.grad.gradient``
 mean-squared error over shard_rows rows, lowered by ``tgcb.runtime``), runs it, and averages
 the four gradients over ranks with NCCL over NVLink (``torch.distributed``; AVG, since every
 shard's loss is a mean over the same number of rows, so the global gradient is the mean of the
-shard gradients). Each gradient's all-reduce is started on a separate stream as soon as the
-launch that finalises it has been queued, so it overlaps the launches that remain.
+shard gradients). By default the four all-reduces are one grouped NCCL call after the last
+launch (``buckets="final"``): the persistent GEMMs hold every SM, so a collective queued beside
+them waits for a gap anyway, and one call pays NCCL's latency once. With
+``buckets="per_gradient"`` each gradient's all-reduce starts on a side stream as soon as the
+launch that finalises it has been queued, overlapping the launches that remain.
 
 The same code runs with the ``gloo`` backend on CPU ranks when ``executor`` replaces the GPU
 plan (tests use the oracle there), which is how the host-side sharding and averaging logic is
