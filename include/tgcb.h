@@ -87,8 +87,10 @@ const char* tgcb_version(void);
 /* Message of the calling thread's last failure ("" if none). */
 const char* tgcb_last_error(void);
 
-/* Select `device`, allocate its status word and resolve the driver's tensor-map encoder.
- * Idempotent per device. Replaces nothing in tgc (tgc is single-device CPU). */
+/* Select `device` (0 .. 15), allocate its status word, resolve the driver's tensor-map encoder
+ * and look up the device address of tgcb_sum_pairwise_f32_noalloc's built-in scratch array.
+ * Idempotent per device; each call repeats the look-up. Replaces nothing in tgc (tgc is
+ * single-device CPU). */
 int tgcb_init(int device);
 
 /* Number of CUDA devices visible (0 on a host without a GPU). Never fails. */
@@ -105,9 +107,13 @@ void tgcb_free(void* p);
 
 /* Load a cubin produced by tgcb_compile_cubin into the current context. */
 int tgcb_module_load(const void* cubin, size_t size, tgcb_module** out);
-/* Waits for the current device (its kernels may still be running), then releases the module.
- * Call it with the device the module's plans ran on current; destroy those plans first. */
-void tgcb_module_unload(tgcb_module* m);
+/* Releases the module once the launches its plans queued have finished: every tgcb_plan_run*
+ * records an event behind its launches, per device and stream, and this call waits for those
+ * events only (other work on the devices keeps running). Destroy the module's plans first.
+ * Returns TGCB_E_CUDA, and keeps the module loaded, when a wait fails (its kernels may still be
+ * running); a plan run captured into a CUDA graph records its event as a graph node, so the
+ * wait covers the graph's last replay. */
+int tgcb_module_unload(tgcb_module* m);
 
 /* Resolve each launch's kernel in `m` and keep the descriptors.
  * Replaces: namespace["compiled"] (tgc/runtime/executor.py:113). */
@@ -191,10 +197,14 @@ int tgcb_sum_sequential_f32(const float* x, uint64_t n, float* out, void* stream
  * library (TGCB_NOALLOC_SCRATCH_BYTES per device, held by every GPU that loads the library
  * until the process exits) instead of caller scratch, and calls no allocator.
  *   - Limit: n must need at most TGCB_NOALLOC_SCRATCH_BYTES of scratch, see
- *     tgcb_sum_pairwise_scratch_bytes(n, block); that is up to 2^28 values at block 8.
+ *     tgcb_sum_pairwise_scratch_bytes(n, block); at block 8 that is up to 9 * 2^25 - 1
+ *     (301,989,887) values.
  *     Larger n is refused with TGCB_E_INVALID before anything is launched.
- *   - The first call on a device looks up the array's device address with that device
- *     current; make that first call before any stream capture.
+ *   - The array's device address is looked up with the device current by tgcb_init(device),
+ *     which allocates a status word of its own; after it, calls on that device do no look-up.
+ *     A caller that never calls tgcb_init gets the look-up in its first call on each device
+ *     (which may load the library's module there); make that first call before any stream
+ *     capture. Devices 0 .. 15, as for tgcb_init.
  *   - Every call shares the one array, so calls whose kernels overlap on the GPU (different
  *     streams, or different host threads) race; serialise them. Nothing in the array has to
  *     start at zero: each level of the tree writes every partial it later reads. */

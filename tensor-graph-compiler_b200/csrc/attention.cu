@@ -20,9 +20,8 @@
 #include <cmath>
 #include <cstdint>
 
+#include "internal.h"
 #include "tgcb.h"
-
-int tgcb_internal_fail(int code, const char* what, const char* detail);
 
 namespace {
 

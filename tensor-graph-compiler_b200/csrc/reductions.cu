@@ -24,10 +24,8 @@
 #include <mutex>
 #include <string>
 
+#include "internal.h"
 #include "tgcb.h"
-
-// Records the calling thread's last error (defined in runtime.cu).
-int tgcb_internal_fail(int code, const char* what, const char* detail);
 
 namespace {
 
@@ -601,15 +599,30 @@ int tgcb_quantise_rows_i8(const float* x, int64_t rows, int64_t cols, int8_t* q,
 //
 // For callers that cannot allocate device memory (see include/tgcb.h): the pairwise sum's
 // partials live in this file-scope device array instead of caller scratch. On the host its
-// name is only a stand-in for the symbol, never a device address; the address is looked up
-// once per device with cudaGetSymbolAddress and then passed to the unchanged entry point.
+// name is only a stand-in for the symbol, never a device address; the address is looked up per
+// device with cudaGetSymbolAddress (by tgcb_init, or by the first call on a device tgcb_init has
+// not set up) and then passed to the unchanged entry point.
 static __device__ __align__(256) unsigned char g_noalloc_pairwise_scratch[TGCB_NOALLOC_SCRATCH_BYTES];
 
 namespace {
-constexpr int kNoAllocDevices = 16;
-void* g_noalloc_scratch_ptr[kNoAllocDevices] = {};
+void* g_noalloc_scratch_ptr[kTgcbMaxDevices] = {};
 std::mutex g_noalloc_mutex;
+
+int noalloc_lookup_locked(int device) {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_pairwise_scratch);
+  if (e != cudaSuccess) return report(TGCB_E_CUDA, "cudaGetSymbolAddress of the built-in scratch array", e);
+  g_noalloc_scratch_ptr[device] = p;
+  return TGCB_OK;
+}
 }  // namespace
+
+int tgcb_internal_noalloc_setup(int device) {
+  if (device < 0 || device >= kTgcbMaxDevices)
+    return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_init", "device index out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  return noalloc_lookup_locked(device);
+}
 
 extern "C" int tgcb_sum_pairwise_f32_noalloc(const float* x, uint64_t n, int block, float* out, void* stream) {
   if (x == nullptr || out == nullptr)
@@ -620,21 +633,19 @@ extern "C" int tgcb_sum_pairwise_f32_noalloc(const float* x, uint64_t n, int blo
   const size_t need = tgcb_sum_pairwise_scratch_bytes(n, block);
   if (need > TGCB_NOALLOC_SCRATCH_BYTES)
     return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_pairwise_f32_noalloc",
-                              "this length needs more scratch than the built-in 1 MiB array (at most 2^28 values at "
-                              "block 8); use tgcb_sum_pairwise_f32 with caller scratch");
+                              "this length needs more scratch than the built-in 1 MiB array (at most 9 * 2^25 - 1 "
+                              "values at block 8); use tgcb_sum_pairwise_f32 with caller scratch");
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return report(TGCB_E_CUDA, "cudaGetDevice", e);
-  if (dev < 0 || dev >= kNoAllocDevices)
+  if (dev < 0 || dev >= kTgcbMaxDevices)
     return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_pairwise_f32_noalloc", "device index out of range");
   void* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
     if (g_noalloc_scratch_ptr[dev] == nullptr) {
-      void* p = nullptr;
-      e = cudaGetSymbolAddress(&p, g_noalloc_pairwise_scratch);
-      if (e != cudaSuccess) return report(TGCB_E_CUDA, "cudaGetSymbolAddress", e);
-      g_noalloc_scratch_ptr[dev] = p;
+      const int rc = noalloc_lookup_locked(dev);  // tgcb_init never ran for this device
+      if (rc != TGCB_OK) return rc;
     }
     scratch = g_noalloc_scratch_ptr[dev];
   }

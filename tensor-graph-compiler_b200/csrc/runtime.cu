@@ -15,6 +15,7 @@
 #include <string>
 #include <vector>
 
+#include "internal.h"
 #include "tgcb.h"
 
 namespace {
@@ -48,7 +49,7 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-constexpr int kMaxDevices = 16;
+constexpr int kMaxDevices = kTgcbMaxDevices;
 struct DeviceState {
   bool ready = false;
   int* status = nullptr;
@@ -83,8 +84,17 @@ int current_state(DeviceState** out) {
 
 int tgcb_internal_fail(int code, const char* what, const char* detail) { return fail(code, "%s: %s", what, detail); }
 
+// A loaded module. Its code is context-independent, so plans may run it on any device and
+// stream. `done` holds, per device and stream it ran on, an event recorded behind the last
+// launches queued there; tgcb_module_unload waits for all of them before releasing the code.
 struct tgcb_module {
+  struct Done {
+    cudaStream_t stream;
+    cudaEvent_t event;
+  };
   cudaLibrary_t lib = nullptr;
+  std::mutex mu;
+  std::vector<Done> done[kMaxDevices];
 };
 
 struct LaunchState {
@@ -102,6 +112,7 @@ struct LaunchState {
 };
 
 struct tgcb_plan {
+  tgcb_module* module = nullptr;
   std::vector<LaunchState> launches;
   uint64_t arena_bytes = 0;
   int input_count = 0;  // graph inputs the kernels read (tgcb_plan_set_input_count); 0: unchecked
@@ -129,6 +140,9 @@ int tgcb_init(int device) {
   if (device < 0 || device >= kMaxDevices) return fail(TGCB_E_INVALID, "device %d out of range", device);
   CUDA_TRY(cudaSetDevice(device));
   DeviceState& st = g_devices[device];
+  // the allocation-free sum's scratch address, looked up here so its calls need no look-up
+  int rc = tgcb_internal_noalloc_setup(device);
+  if (rc != TGCB_OK) return rc;
   if (st.ready) return TGCB_OK;
   if (st.status == nullptr) CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&st.status), 256));  // kept if a later step fails
   CUDA_TRY(cudaMemset(st.status, 0, 256));
@@ -202,14 +216,27 @@ int tgcb_module_load(const void* cubin, size_t size, tgcb_module** out) {
   return TGCB_OK;
 }
 
-void tgcb_module_unload(tgcb_module* m) {
-  if (m == nullptr) return;
-  // kernels of this module queued on the current device may still be running: let them finish
-  // before their code is released
-  cudaDeviceSynchronize();
-  cudaGetLastError();
-  if (m->lib) cudaLibraryUnload(m->lib);
+int tgcb_module_unload(tgcb_module* m) {
+  if (m == nullptr) return TGCB_OK;
+  // Kernels of this module queued by the last plan run on each device and stream may still be
+  // running: wait for exactly those (not for whole devices), then release the code.
+  int rc = TGCB_OK;
+  for (int d = 0; d < kMaxDevices; ++d) {
+    for (const tgcb_module::Done& x : m->done[d]) {
+      cudaError_t e = cudaEventSynchronize(x.event);
+      if (e != cudaSuccess && rc == TGCB_OK)
+        rc = fail(TGCB_E_CUDA, "waiting for the module's last launches on device %d: %s", d, cudaGetErrorString(e));
+      cudaEventDestroy(x.event);
+    }
+    m->done[d].clear();
+  }
+  if (rc != TGCB_OK) return rc;  // the code stays loaded: a kernel may still be using it
+  if (m->lib) {
+    cudaError_t e = cudaLibraryUnload(m->lib);
+    if (e != cudaSuccess) rc = fail(TGCB_E_CUDA, "cudaLibraryUnload: %s", cudaGetErrorString(e));
+  }
   delete m;
+  return rc;
 }
 
 int tgcb_plan_create(tgcb_module* m, const tgcb_launch_desc* launches, int n_launches, uint64_t arena_bytes,
@@ -217,6 +244,7 @@ int tgcb_plan_create(tgcb_module* m, const tgcb_launch_desc* launches, int n_lau
   if (m == nullptr || out == nullptr || n_launches < 0 || (n_launches > 0 && launches == nullptr))
     return fail(TGCB_E_INVALID, "tgcb_plan_create: bad arguments");
   auto* p = new tgcb_plan();
+  p->module = m;
   p->arena_bytes = arena_bytes;
   p->launches.resize(n_launches);
   for (int i = 0; i < n_launches; ++i) {
@@ -391,6 +419,55 @@ int launch_one(DeviceState* st, LaunchState& ls, TgcbArgs& args, void* arena, co
   return TGCB_OK;
 }
 
+// Record, behind the launches just queued on `s`, the module's completion event for the current
+// device and this stream (created on first use). Inside a stream capture the record becomes a
+// node of the graph (cudaEventRecordExternal), so every replay of the graph marks it.
+int mark_done(tgcb_module* m, cudaStream_t s) {
+  int dev = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(TGCB_E_INVALID, "device %d out of range", dev);
+  cudaEvent_t ev = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(m->mu);
+    std::vector<tgcb_module::Done>& list = m->done[dev];
+    for (const tgcb_module::Done& x : list)
+      if (x.stream == s) ev = x.event;
+    if (ev == nullptr) {
+      if (list.size() >= 16) {
+        // many streams: forget the events whose work has finished
+        size_t k = 0;
+        for (const tgcb_module::Done& x : list) {
+          if (cudaEventQuery(x.event) == cudaSuccess)
+            cudaEventDestroy(x.event);
+          else
+            list[k++] = x;
+        }
+        list.resize(k);
+        cudaGetLastError();  // a query that answered "not ready" leaves that status behind
+      }
+      CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+      list.push_back({s, ev});
+    }
+  }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  CUDA_TRY(cudaStreamIsCapturing(s, &cs));
+  if (cs == cudaStreamCaptureStatusActive)
+    CUDA_TRY(cudaEventRecordWithFlags(ev, s, cudaEventRecordExternal));
+  else
+    CUDA_TRY(cudaEventRecord(ev, s));
+  return TGCB_OK;
+}
+
+// Ends a plan run: marks the module's completion on `s` behind whatever was queued, also when a
+// launch failed part way (the launches before it are in flight), keeping the first error.
+int finish_run(tgcb_plan* p, cudaStream_t s, int rc) {
+  if (rc == TGCB_OK) return mark_done(p->module, s);
+  const std::string first = g_last_error;
+  mark_done(p->module, s);
+  g_last_error = first;
+  return rc;
+}
+
 __global__ void delay_kernel(unsigned long long ns) {
   unsigned long long start;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(start));
@@ -414,9 +491,9 @@ int tgcb_plan_run(tgcb_plan* p, void* arena, const void* const* inputs, int n_in
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   for (LaunchState& ls : p->launches) {
     rc = launch_one(st, ls, args, arena, inputs, n_inputs, s);
-    if (rc != TGCB_OK) return rc;
+    if (rc != TGCB_OK) break;
   }
-  return TGCB_OK;
+  return finish_run(p, s, rc);
 }
 
 int tgcb_plan_run_range(tgcb_plan* p, int first, int count, void* arena, const void* const* inputs, int n_inputs,
@@ -431,9 +508,9 @@ int tgcb_plan_run_range(tgcb_plan* p, int first, int count, void* arena, const v
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   for (int i = first; i < first + count; ++i) {
     rc = launch_one(st, p->launches[i], args, arena, inputs, n_inputs, s);
-    if (rc != TGCB_OK) return rc;
+    if (rc != TGCB_OK) break;
   }
-  return TGCB_OK;
+  return finish_run(p, s, rc);
 }
 
 int tgcb_plan_run_profiled(tgcb_plan* p, void* arena, const void* const* inputs, int n_inputs, void* stream,
@@ -463,6 +540,7 @@ int tgcb_plan_run_profiled(tgcb_plan* p, void* arena, const void* const* inputs,
     cudaError_t err = cudaEventRecord(ev[i + 1], s);
     if (err != cudaSuccess) rc = fail(TGCB_E_CUDA, "cudaEventRecord: %s", cudaGetErrorString(err));
   }
+  rc = finish_run(p, s, rc);
   if (rc == TGCB_OK) {
     cudaError_t err = cudaStreamSynchronize(s);
     if (err != cudaSuccess) rc = fail(TGCB_E_CUDA, "cudaStreamSynchronize: %s", cudaGetErrorString(err));

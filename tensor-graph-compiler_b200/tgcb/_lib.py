@@ -76,7 +76,7 @@ SIGNATURES = {
     ),
     "tgcb_free": (None, [ctypes.c_void_p]),
     "tgcb_module_load": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
-    "tgcb_module_unload": (None, [ctypes.c_void_p]),
+    "tgcb_module_unload": (ctypes.c_int, [ctypes.c_void_p]),
     "tgcb_plan_create": (
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.POINTER(LaunchDesc), ctypes.c_int, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)],

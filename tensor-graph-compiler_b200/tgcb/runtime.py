@@ -306,16 +306,23 @@ class CompiledGraph:
         self.function: Callable = self._run
         self.launches_per_call = len(module.launches)
 
+    def close(self) -> None:
+        """Release the plan and the module. The module's code is released only after the
+        launches of this graph's last calls have finished (tgcb_module_unload waits for the
+        events those calls recorded on their streams, not for the whole device); raises
+        ``DeviceError`` if that wait fails, in which case the code stays loaded."""
+        lib = _lib.load()
+        plan, self._plan = getattr(self, "_plan", None), None
+        if plan:
+            lib.tgcb_plan_destroy(plan)
+        module, self._module = getattr(self, "_module", None), None
+        if module:
+            _lib.check(lib.tgcb_module_unload(module), "unloading the generated module")
+
     def __del__(self):
         try:
-            lib = _lib.load()
-            if getattr(self, "_plan", None):
-                lib.tgcb_plan_destroy(self._plan)
-            if getattr(self, "_module", None):
-                # the unload waits for this device: the last call's kernels may still be running
-                with self._torch.cuda.device(self.device):
-                    lib.tgcb_module_unload(self._module)
-        except Exception:  # noqa: BLE001 - interpreter shutdown
+            self.close()
+        except Exception:  # noqa: BLE001 - nothing can be raised from a finaliser
             pass
 
     @property

@@ -55,6 +55,26 @@ def test_matches_the_scratch_taking_entry_point_twice(cuda, n, block):
         assert _without_allocation(lib, x, block, out) == expected
 
 
+# The longest inputs the built-in array accepts. At block 1, 2^26 - 1 values split into 2^25
+# irregular leaves whose partials fill more than half of the array, so the last combining
+# levels sit at its far end; at block 8, 9 * 2^25 - 1 values is the longest length whose
+# partials still fit (one more value adds a level and needs more than the whole array).
+@pytest.mark.parametrize("n,block", [((1 << 26) - 1, 1), (9 * (1 << 25) - 1, 8)])
+def test_longest_accepted_lengths_match_bit_for_bit(cuda, n, block):
+    lib = _lib.load()
+    _lib.ensure_device(0)
+    need = lib.tgcb_sum_pairwise_scratch_bytes(n, block)
+    assert SCRATCH_LIMIT // 2 < need <= SCRATCH_LIMIT
+    assert lib.tgcb_sum_pairwise_scratch_bytes(n + 1, block) > SCRATCH_LIMIT
+    out = torch.empty(1, dtype=torch.float32, device=cuda)
+    for seed in (3, 4):
+        g = torch.Generator(device=cuda).manual_seed(seed)
+        x = torch.rand(n, generator=g, device=cuda)
+        expected = _with_caller_scratch(lib, x, block)
+        assert _without_allocation(lib, x, block, out) == expected
+        del x
+
+
 def test_refuses_lengths_beyond_the_built_in_scratch(cuda):
     lib = _lib.load()
     _lib.ensure_device(0)
