@@ -134,6 +134,17 @@ class RowGroup:
     phase: dict[str, int] = field(default_factory=dict)
 
 
+def col_split(rows: int, cols: int) -> tuple[int, int]:
+    """(parts, rows per part) of a column reduction over [rows, cols]: enough row blocks for about
+    eight CTAs of 256 columns per SM, at least 16 rows each. The parts are [k L, (k + 1) L), so the
+    order is tgc's split_sum(column, parts) (tgc/passes/reduction.py:105-121): ceil(rows / parts)
+    is L again for every L of this form."""
+    cblocks = (cols + 255) // 256
+    parts = max(1, min((rows + 15) // 16, (NUM_SMS * 8 + cblocks - 1) // cblocks))
+    per = (rows + parts - 1) // parts
+    return (rows + per - 1) // per, per
+
+
 def _prod(xs) -> int:
     p = 1
     for x in xs:
@@ -899,10 +910,7 @@ class Lowering:
         t = ctype(node.output.dtype)
         opn = node.op.name
         cblocks = (C + 255) // 256
-        # enough row blocks for ~8 CTAs per SM; each thread keeps UNROLL loads in flight
-        P = max(1, min((R + 15) // 16, (NUM_SMS * 8 + cblocks - 1) // cblocks))
-        L = (R + P - 1) // P
-        P = (R + L - 1) // L
+        P, L = col_split(R, C)
         scratch = f"{name}__partials"
         self.scratch[scratch] = P * C * 8
         k1, k2 = self._kname("colpart"), self._kname("colfinal")

@@ -24,7 +24,7 @@ from __future__ import annotations
 
 from collections.abc import Callable
 
-from tgcb import grad, ir, workloads
+from tgcb import collective, grad, ir, workloads
 from tgcb.errors import ConfigError, PassError
 
 GRADS = ("w1", "b1", "w2", "b2")
@@ -43,15 +43,13 @@ def shard_rows(total_rows: int, devices: int, rank: int) -> tuple[int, int]:
 
 
 def ring_time(size_bytes: int, devices: int, bytes_per_second: float, latency_seconds: float) -> float:
-    """tgc's ring all-reduce model (collective.py:76-88) with a given link: 2(n-1) steps of size/n."""
-    if devices <= 1:
-        return 0.0
-    return 2 * (devices - 1) * (latency_seconds + (size_bytes / devices) / bytes_per_second)
+    """tgc's ring all-reduce model (collective.py:76-88) on a link of the given bandwidth and latency."""
+    return collective.ring_time(size_bytes, devices, collective.Link("given", bytes_per_second, latency_seconds))
 
 
 def ring_volume(size_bytes: int, devices: int) -> float:
     """Bytes each device sends in a ring all-reduce (collective.py:113-122)."""
-    return 0.0 if devices <= 1 else 2.0 * size_bytes * (devices - 1) / devices
+    return collective.ring_volume(size_bytes, devices)
 
 
 def train_graph(rows: int, d: int = 1024, f: int = 4096):
