@@ -61,6 +61,8 @@ def parse_args():
     p.add_argument("--workload", choices=["mlp", "cone", "int8", "longsum", "train"], default="mlp")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--only", action="store_true", help="time the chosen workload alone, without the others under 'workloads'")
+    p.add_argument("--sub-steps", type=int, default=0, help="timed steps of each nested workload (default: --steps)")
     p.add_argument("--train-rows", type=int, default=65536, help="global batch of the train workload (profiling uses a small one)")
     p.add_argument("--train-buckets", choices=["final", "per_gradient"], default="final",
                    help="train: one grouped gradient all-reduce after the backward, or one per gradient as it becomes final")
@@ -373,6 +375,7 @@ class GraphWorkload:
 class MlpWorkload(GraphWorkload):
     name = "mlp"
     dtype = "tf32"
+    machine_kind = "tf32"
     rows = 8192
 
     def graph(self):
@@ -398,6 +401,7 @@ class MlpWorkload(GraphWorkload):
 class ConeWorkload(GraphWorkload):
     name = "cone"
     dtype = "f32"
+    machine_kind = "fp32"
 
     def graph(self):
         from tgcb import ir, workloads
@@ -416,6 +420,69 @@ class ConeWorkload(GraphWorkload):
             "l2": L2_NOTE,
         }
 
+    def extras(self, runner, steps: int) -> dict:
+        """The launch's ceiling, the outputs' error against float64, and tgc's fusion plans.
+
+        Ceiling: the same launch shape reading the same 16 MiB and only adding it up (a row sum
+        over x, compiled by the same codegen), timed the same way; what any kernel over these
+        bytes in one launch reaches here. Errors: each output's largest relative difference
+        from the same computation in float64 (torch, on the GPU). Plans: tgc's fusion search
+        (tgcb.fusion_search) on this graph, every strategy priced by tgc's rules and turned into
+        time on the B200 roofline, beside the backend's one-pass kernel.
+        """
+        import torch
+
+        from tgcb import cost, fusion_search, ir, workloads
+        from tgcb.runtime import compile_graph
+
+        ceiling = compile_graph(workloads.row_sum_graph(ir.Builder), device=runner.device.index)
+        arena = ceiling.new_arena()
+        feeds = {"x": self.dev_feeds["x"]}
+        for _ in range(3):
+            ceiling.run_profiled(arena, feeds)
+        ceiling_ms = runner.max_over_ranks(sum(runner.timed(lambda: ceiling.run_profiled(arena, feeds)[1], steps))) / steps
+        cone_ms = runner.max_over_ranks(sum(runner.timed(self.step_profiled, steps))) / steps
+        outs = self.compiled.function(self.arena, self.dev_feeds)
+        x = self.dev_feeds["x"].double()
+        t = torch.exp(x * 0.5 + (-1.0))
+        ref = (t.sum(1), t.amax(1), (t * x).sum(1))
+        names = ("row_sum", "row_max", "row_sum_tx")
+        errors = {k: float(((o.double() - r).abs() / r.abs()).max()) for k, o, r in zip(names, outs, ref, strict=True)}
+        if runner.rank != 0:
+            return {}
+        machine = cost.b200(runner.peaks, "fp32")
+        dag, _ = fusion_search.dag_of(self.g)
+        plans = []
+        for row in fusion_search.compare(dag):
+            plan = fusion_search.FusionPlan(frozenset(row["materialised"]), row["groups"], row["flops"], row["traffic"])
+            secs = fusion_search.predicted_seconds(plan, machine.flops_per_second, machine.bytes_per_second)
+            plans.append({**{k: row[k] for k in ("strategy", "groups", "flops", "traffic", "cost")},
+                          "predicted_us": round(secs * 1e6, 3)})
+        best_tgc = min((p for p in plans if not p["strategy"].startswith("one pass")), key=lambda p: p["cost"])
+        one = next(p for p in plans if p["strategy"].startswith("one pass"))
+        return {
+            "ceiling": {
+                "kernel": "tgcb_row_1 of row_sum over the same x (same grid, block and bytes; only adds)",
+                "ceiling_us": round(ceiling_ms * 1e3, 2),
+                "cone_us": round(cone_ms * 1e3, 2),
+                "cone_over_ceiling": round(ceiling_ms / cone_ms, 4),
+                "ceiling_gbs": round(16 * 2**20 / (ceiling_ms * 1e-3) / 1e9, 1),
+                "note": "both timed back to back here with L2 flushed; a 16 MiB launch is bound by launch ramp and "
+                        "drain, not by HBM (64 MiB and 256 MiB reads reach higher fractions)",
+            },
+            "error_vs_fp64": {**{k: {"max_rel_error": v} for k, v in errors.items()},
+                              "declared_bracketing": "row tree (tgcb_row_1): bit-exact to oracle/bracketing.c "
+                                                     "oracle_row_tree in the GPU tests, i.e. zero error against the "
+                                                     "chosen bracketing"},
+            "fusion_search": {
+                "machine": machine.as_dict(),
+                "plans": plans,
+                "best_tgc_plan": best_tgc["strategy"],
+                "predicted_speedup_of_one_pass_over_best_tgc_plan": round(best_tgc["predicted_us"] / one["predicted_us"], 3),
+                "model_cost_regret_of_best_tgc_plan": round(best_tgc["cost"] / one["cost"], 4),
+            },
+        }
+
 
 class Int8Workload(GraphWorkload):
     """The int8 linear layer as a serving step: the float32 activations are quantised per token
@@ -426,6 +493,7 @@ class Int8Workload(GraphWorkload):
 
     name = "int8"
     dtype = "int8 x int8 -> int32, f32 dequant"
+    machine_kind = "int8"
     rows, k, n = 8192, 4096, 4096
 
     def graph(self):
@@ -636,6 +704,54 @@ class LongSumWorkload:
         ev[2].synchronize()
         return [ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])]
 
+    def extras(self, runner, steps: int) -> dict:
+        """The sequential schedule's latency, and both schedules' error against float64.
+
+        Sequential: one chain of 2^26 dependent additions, so its time is latency, not
+        bandwidth; timed 3 times (L2 flushed). Errors: on this rank's 2^26-value vector (rank 0
+        holds the seed-0 vector of the long-sum workload), the pairwise and sequential results
+        against the correctly rounded float64 sum (tgcb.summation.exact, tgc's summation.exact).
+        """
+        import torch
+
+        from tgcb import summation
+
+        seq_out = torch.empty(1, dtype=torch.float32, device=runner.device)
+        pw_out = torch.empty(1, dtype=torch.float32, device=runner.device)
+
+        def seq_step():
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            summation.sequential_into(self.dev, seq_out)
+            e.record()
+            e.synchronize()
+            return [s.elapsed_time(e)]
+
+        seq_step()
+        seq_ms = runner.max_over_ranks(runner.timed(seq_step, 3)[0]) / 3
+        summation.pairwise_into(self.dev, pw_out, self.scratch)
+        torch.cuda.synchronize()
+        if runner.rank != 0:
+            return {}
+        exact = summation.exact(self.dev)
+        pw, sq = float(pw_out.item()), float(seq_out.item())
+        return {
+            "sequential": {
+                "ms": round(seq_ms, 3),
+                "gbs": round(self.n * 4 / (seq_ms * 1e-3) / 1e9, 2),
+                "bound": "latency: one chain of 2^26 dependent float adds on one thread",
+                "kernel": "sequential_chain",
+            },
+            "error_vs_fp64": {
+                "vector": "rank 0's 2^26 values (the long-sum workload's seed-0 input)",
+                "exact_fp64": exact,
+                "pairwise": {"value": pw, "rel_error": summation.relative_error(pw, exact)},
+                "sequential": {"value": sq, "rel_error": summation.relative_error(sq, exact)},
+                "declared_bracketing": "both schedules are bit-exact to tgc's summation.pairwise / sequential "
+                                       "(tests), i.e. zero error against the chosen bracketing",
+            },
+        }
+
     def step_e2e(self) -> None:
         from tgcb import summation
 
@@ -680,6 +796,7 @@ class TrainWorkload:
     name = "train"
     unit = "train steps/s"
     dtype = "tf32"
+    machine_kind = "tf32"
     scaling = "strong"
     buckets = "final"
     global_rows = 65536
@@ -753,6 +870,61 @@ class TrainWorkload:
             {"name": "exposed NCCL all-reduce and gaps", "kind": "allreduce", "bound": "nvlink", "work": self.payload}
         ]
 
+    def extras(self, runner, steps: int) -> dict:
+        """On 2+ GPUs: the gradient all-reduce alone, measured, beside tgc's all-reduce model.
+
+        The 33,574,912-byte gradient set is all-reduced (NCCL AVG) as one flat buffer, 10 times
+        after 3 warm-ups, each event-timed, max over ranks; a one-float all-reduce gives the
+        start-up latency. tgc's ring model (tgcb.collective, collective.py:76-379) on an NVLink
+        link of the measured 770 GB/s peer-copy bandwidth, with the measured start-up divided
+        over the ring's 2(n-1) messages, predicts the same all-reduce, and the four gradients
+        reduced one call each.
+        """
+        import torch
+
+        from tgcb import collective
+
+        n, dist = runner.n, runner.dist
+        if n == 1 or dist is None:
+            return {}
+        flat = torch.zeros(self.payload // 4, dtype=torch.float32, device=runner.device)
+        one = torch.zeros(1, dtype=torch.float32, device=runner.device)
+
+        def timed_ar(t, reps):
+            for _ in range(3):
+                dist.all_reduce(t, op=dist.ReduceOp.AVG)
+            total = 0.0
+            for _ in range(reps):
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                dist.all_reduce(t, op=dist.ReduceOp.AVG)
+                e.record()
+                e.synchronize()
+                total += s.elapsed_time(e)
+            return runner.max_over_ranks(total) / reps
+
+        big_ms = timed_ar(flat, 10)
+        tiny_ms = timed_ar(one, 10)
+        if runner.rank != 0:
+            return {}
+        link = collective.nvlink(latency_seconds=tiny_ms * 1e-3 / (2 * (n - 1)))
+        grads = [1024 * 4096 * 4, 4096 * 4, 4096 * 1024 * 4, 1024 * 4]
+        return {
+            "allreduce": {
+                "bytes": self.payload,
+                "measured_us": round(big_ms * 1e3, 2),
+                "measured_busbw_gbs": round(collective.bus_bandwidth(self.payload, n, big_ms * 1e-3) / 1e9, 1),
+                "one_float_us": round(tiny_ms * 1e3, 2),
+                "link": link.as_dict(),
+                "model_ring_us": round(collective.ring_time(self.payload, n, link) * 1e6, 2),
+                "model_tree_us": round(collective.tree_time(self.payload, n, link) * 1e6, 2),
+                "model_four_calls_us": round(collective.bucket_time(grads, n, link) * 1e6, 2),
+                "model_ring_volume_bytes": collective.ring_volume(self.payload, n),
+                "how": "NCCL AVG over one flat buffer of the gradient set's size; the step itself reduces the four "
+                       "gradients in one grouped call after the backward",
+            }
+        }
+
     def cpu_program(self):
         """One 8192-row shard of the step by the oracle (the full 65536 rows take minutes on a CPU)."""
         from oracle import interp
@@ -768,6 +940,8 @@ class TrainWorkload:
 
 WORKLOADS = {"mlp": MlpWorkload, "cone": ConeWorkload, "int8": Int8Workload, "longsum": LongSumWorkload,
              "train": TrainWorkload}
+# timed after the headline workload in the same run, each reported under "workloads"
+SUB_WORKLOADS = ("cone", "longsum", "int8", "train")
 
 
 # ----------------------------------------------------------------------------- cpu baseline
@@ -844,6 +1018,244 @@ def main() -> int:
         json_out.flush()
 
 
+class Runner:
+    """What every workload's measurement shares: device, process group, L2 flush, timing."""
+
+    def __init__(self, args, device, dist, n: int, rank: int, local: int):
+        import torch
+
+        self.args, self.device, self.dist, self.n, self.rank, self.local = args, device, dist, n, rank, local
+        self.flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+        self.flush_read = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+        self.flush_sink = torch.empty((), dtype=torch.float32, device=device)
+        self.peaks, self.peak_source = peaks()
+
+    def flush_l2(self) -> None:
+        import torch
+
+        self.flush.zero_()
+        torch.sum(self.flush_read, dim=0, out=self.flush_sink)
+
+    def timed(self, fn, steps: int) -> list[float]:
+        """``steps`` calls of ``fn`` (which returns ms per launch), each after an L2 flush and a
+        bounded delay kernel; returns the per-launch ms summed over the steps."""
+        from tgcb.runtime import delay
+
+        total = None
+        for _ in range(steps):
+            self.flush_l2()
+            delay(50_000)
+            ms = fn()
+            total = ms if total is None else [a + b for a, b in zip(total, ms, strict=True)]
+        return total
+
+    def max_over_ranks(self, value: float) -> float:
+        import torch
+
+        if not self.dist:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=self.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier(self) -> None:
+        import torch
+
+        torch.cuda.synchronize()
+        if self.dist:
+            self.dist.barrier()
+        torch.cuda.synchronize()
+
+
+def make_workload(name: str, runner: Runner):
+    wl = WORKLOADS[name](runner.rank)
+    if name == "train":
+        wl.global_rows = runner.args.train_rows
+        wl.buckets = runner.args.train_buckets
+        wl.setup(runner.device, runner.dist, runner.n)
+    elif name == "longsum":
+        wl.setup(runner.device, runner.dist, runner.n)
+    else:
+        wl.setup(runner.device)
+    return wl
+
+
+def roofline_of(wl, runner: Runner, per_launch: list[float], steps: int, clocks: dict) -> tuple[dict, list[dict]]:
+    pk, src = runner.peaks, runner.peak_source
+    work = wl.kernel_work()
+    dom = max((i for i in range(len(per_launch)) if work[i]["bound"] != "nvlink"), key=lambda i: per_launch[i])
+    dk = work[dom]
+    avg_ms = per_launch[dom] / steps
+    if dk["bound"] == "tensor":
+        factor = 0.5 if dk.get("type") == "tf32" else 2.0
+        # The burst cuBLAS rate was measured at full clocks, the sustained one under the power
+        # cap at lower clocks: compare against the one whose clocks this run actually had.
+        sm, sm_max = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
+        burst = bool(sm and sm_max and sm >= 0.95 * sm_max)
+        key = "bf16_tflops" if burst else "bf16_tflops_sustained"
+        peak = pk[key] * factor
+        achieved = dk["work"] / (avg_ms * 1e-3) / 1e12
+        unit = "TFLOP/s" if dk.get("type") == "tf32" else "TOP/s"
+        peak_note = (
+            f"{'tf32' if factor == 0.5 else 'int8'} dense rate taken as {factor}x the {src} "
+            f"{'burst' if burst else 'sustained'} bf16 cuBLAS rate ({pk[key]} TF/s, MEASURED_PEAKS.json {key}; "
+            f"{'SM clocks stayed at max during the timed region' if burst else 'SM clocks dropped during the timed region'}); "
+            "B200 dense tf32:bf16:int8 = 1:2:4"
+        )
+    else:
+        peak = pk["hbm_gbs"]
+        achieved = dk["work"] / (avg_ms * 1e-3) / 1e9
+        unit = "GB/s"
+        peak_note = f"{src} STREAM-style copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"
+    roof = {
+        "bound": dk["bound"],
+        "kernel": dk["name"],
+        "achieved": round(achieved, 2),
+        "peak": round(peak, 1),
+        "unit": unit,
+        "frac": round(achieved / peak, 4),
+        "traffic": read_traffic(wl.name, dk["name"]),
+        "peak_source": peak_note,
+        **({"also": dk["also"]} if dk.get("also") else {}),
+    }
+    return roof, work
+
+
+def model_block(wl, runner: Runner, ms_per_step: float) -> dict | None:
+    """tgc's roofline model (tgcb.cost) of the step on a B200 machine made from the measured
+    peaks, beside the measured time: tgc's own fused-bytes estimate of the graph, and the
+    same roofline over the bytes the backend's kernel steps move."""
+    from tgcb import cost
+
+    if not hasattr(wl, "compiled") or not hasattr(wl.compiled, "lowering"):
+        return None
+    machine = cost.b200(runner.peaks, getattr(wl, "machine_kind", "fp32"))
+    tgc_est = cost.estimate(wl.compiled.graph, machine)
+    plan = cost.plan_estimate(wl.compiled, machine)
+    return {
+        "machine": machine.as_dict(),
+        "tgc_estimate_us": round(tgc_est.seconds * 1e6, 2),
+        "tgc_estimate": tgc_est.as_dict(),
+        "backend_bytes_estimate_us": round(plan.seconds * 1e6, 2),
+        "measured_us": round(ms_per_step * 1e3, 2),
+        "measured_over_backend_estimate": round(ms_per_step * 1e-3 / plan.seconds, 3) if plan.seconds else None,
+    }
+
+
+def measure(name: str, runner: Runner, steps: int, warmup: int, with_cpu: bool) -> dict | None:
+    """Set up one workload, time it (device events, L2 flushed, max over ranks), time its
+    end-to-end path, and return rank 0's result (None on the other ranks)."""
+    import torch
+
+    args, n, rank, dist = runner.args, runner.n, runner.rank, runner.dist
+    wl = make_workload(name, runner)
+    scaling = getattr(wl, "scaling", "weak")
+    units = wl.units_per_step(n) if hasattr(wl, "units_per_step") else n
+
+    sampler = NvmlClockSampler(runner.local)
+    if not sampler.start():
+        sampler = ClockSampler(runner.local)
+        sampler.start()
+    warm = max(warmup, 3)
+    for _ in range(warm):
+        wl.step_profiled()
+    runner.barrier()
+    sampler.mark_start()
+    per_launch = runner.timed(wl.step_profiled, steps)
+    torch.cuda.synchronize()
+    sampler.mark_end()
+    clocks = sampler.stop()
+    if hasattr(wl, "compiled"):
+        wl.compiled.check_status()
+    total_ms = runner.max_over_ranks(sum(per_launch))
+
+    # end to end through the public API with host buffers
+    for _ in range(2):
+        wl.step_e2e()
+    if hasattr(wl, "run_e2e"):
+        wl.run_e2e(2)
+    runner.barrier()
+    e2e_ms = 0.0
+    stream = torch.cuda.current_stream()
+    if hasattr(wl, "run_e2e"):
+        e2e_ms = wl.run_e2e(steps)
+    else:
+        for _ in range(steps):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            wl.step_e2e()
+            e.record(stream)
+            e.synchronize()
+            e2e_ms += s.elapsed_time(e)
+    e2e_ms = runner.max_over_ranks(e2e_ms)
+    runner.barrier()
+    extras = wl.extras(runner, steps) if hasattr(wl, "extras") else {}
+
+    result = None
+    if rank == 0:
+        roof, work = roofline_of(wl, runner, per_launch, steps, clocks)
+        shares = [p / sum(per_launch) for p in per_launch]
+        value = units * steps / (total_ms * 1e-3)
+        hbm_bytes = sum(w["work"] for w in work if w["bound"] == "hbm")
+        hbm_ms = sum(per_launch[i] for i, w in enumerate(work) if w["bound"] == "hbm") / steps
+        if hasattr(wl, "parallelism"):
+            parallelism = wl.parallelism(n)
+        elif name == "train":
+            parallelism = f"dp{n}: {wl.global_rows // n} rows per GPU, gradients averaged by NCCL all-reduce " + (
+                "as one grouped call after the backward" if args.train_buckets == "final"
+                else "per gradient, overlapped with the backward")
+        else:
+            parallelism = f"dp{n}: independent row shards per GPU, no collective"
+        result = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": wl.unit,
+            "n_gpus": n,
+            "steps": steps,
+            "warmup": warm,
+            "ms_per_step": round(total_ms / steps, 4),
+            "higher_is_better": True,
+            "scaling": scaling,
+            "vs_baseline": None,
+            "dtype": wl.dtype,
+            "data": "synthetic: seeded torch.randn inputs and random-init weights of the workload's shapes",
+            "config": {**wl.config(), "parallelism": parallelism},
+            "roofline": roof,
+            "hbm_kernels": {
+                "algorithmic_bytes_per_exec": hbm_bytes,
+                "achieved_gbs": round(hbm_bytes / (hbm_ms * 1e-3) / 1e9, 1) if hbm_ms > 0 else None,
+                "frac_of_measured_hbm": round(hbm_bytes / (hbm_ms * 1e-3) / 1e9 / runner.peaks["hbm_gbs"], 4)
+                if hbm_ms > 0 else None,
+            },
+            "kernels": [
+                {"name": w["name"], "kind": w["kind"], "avg_ms": round(per_launch[i] / steps, 4), "share": round(shares[i], 4)}
+                for i, w in enumerate(work)
+            ],
+            "e2e": {
+                "value": round(units * steps / (e2e_ms * 1e-3), 3),
+                "unit": wl.unit,
+                "h2d_bytes_per_step": wl.h2d_bytes(),
+                "d2h_bytes_per_step": wl.d2h_bytes(),
+                "how": ("compiled.function(arena, pinned host feeds, stream) then a copy of every output to pinned host "
+                        "memory, calls alternating two streams and two arenas so copies overlap the neighbouring calls"
+                        if hasattr(wl, "run_e2e") else "one call at a time: pinned host inputs copied in, result copied out"),
+            },
+            "gpu_launches": steps * wl.launches_per_step(),
+            "clocks": clocks,
+        }
+        model = model_block(wl, runner, total_ms / steps)
+        if model:
+            result["model"] = model
+        result.update(extras or {})
+        if with_cpu:
+            result["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
+    del wl
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    runner.barrier()
+    return result
+
+
 def _main(json_out) -> int:
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -866,172 +1278,22 @@ def _main(json_out) -> int:
 
         import torch.distributed as dist_mod
 
+        # communicator set-up lines on stderr: which ranks joined, over which transport
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist_mod.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
         dist = dist_mod
 
-    wl = WORKLOADS[args.workload](rank)
-    if args.workload == "train":
-        wl.global_rows = args.train_rows
-        wl.buckets = args.train_buckets
-        wl.setup(device, dist, n)
-    elif args.workload == "longsum":
-        wl.setup(device, dist, n)
-    else:
-        wl.setup(device)
-    scaling = getattr(wl, "scaling", "weak")
-    units = wl.units_per_step(n) if hasattr(wl, "units_per_step") else n
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
-    flush_read = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
-    flush_sink = torch.empty((), dtype=torch.float32, device=device)
-
-    def flush_l2():
-        flush.zero_()
-        torch.sum(flush_read, dim=0, out=flush_sink)
-
-    from tgcb.runtime import delay
-
-    sampler = NvmlClockSampler(local)
-    if not sampler.start():
-        sampler = ClockSampler(local)
-        sampler.start()
-    warm = max(args.warmup, 3)
-    for _ in range(warm):
-        wl.step_profiled()
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-
-    sampler.mark_start()
-    per_launch = None
-    step_ms = []
-    for _ in range(args.steps):
-        flush_l2()
-        delay(50_000)
-        ms = wl.step_profiled()
-        step_ms.append(sum(ms))
-        per_launch = ms if per_launch is None else [a + b for a, b in zip(per_launch, ms, strict=True)]
-    torch.cuda.synchronize()
-    sampler.mark_end()
-    clocks = sampler.stop()
-    if hasattr(wl, "compiled"):
-        wl.compiled.check_status()
-    total_ms = sum(step_ms)
-    if dist:
-        dist.barrier()
-        t = torch.tensor([total_ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-
-    # end to end through the public API with host buffers
-    for _ in range(2):
-        wl.step_e2e()
-    if hasattr(wl, "run_e2e"):
-        wl.run_e2e(2)
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    e2e_ms = 0.0
-    stream = torch.cuda.current_stream()
-    if hasattr(wl, "run_e2e"):
-        e2e_ms = wl.run_e2e(args.steps)
-    else:
-        for _ in range(args.steps):
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record(stream)
-            wl.step_e2e()
-            e.record(stream)
-            e.synchronize()
-            e2e_ms += s.elapsed_time(e)
-    if dist:
-        t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-        dist.barrier()
-
-    result = None
-    if rank == 0:
-        pk, src = peaks()
-        work = wl.kernel_work()
-        shares = [p / sum(per_launch) for p in per_launch]
-        dom = max((i for i in range(len(per_launch)) if work[i]["bound"] != "nvlink"), key=lambda i: per_launch[i])
-        dk = work[dom]
-        avg_ms = per_launch[dom] / args.steps
-        if dk["bound"] == "tensor":
-            factor = 0.5 if dk.get("type") == "tf32" else 2.0
-            # The burst cuBLAS rate was measured at full clocks, the sustained one under the power
-            # cap at lower clocks: compare against the one whose clocks this run actually had.
-            sm, sm_max = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
-            burst = bool(sm and sm_max and sm >= 0.95 * sm_max)
-            key = "bf16_tflops" if burst else "bf16_tflops_sustained"
-            peak = pk[key] * factor
-            achieved = dk["work"] / (avg_ms * 1e-3) / 1e12
-            unit = "TFLOP/s" if dk.get("type") == "tf32" else "TOP/s"
-            peak_note = (
-                f"{'tf32' if factor == 0.5 else 'int8'} dense rate taken as {factor}x the {src} "
-                f"{'burst' if burst else 'sustained'} bf16 cuBLAS rate ({pk[key]} TF/s, MEASURED_PEAKS.json {key}; "
-                f"{'SM clocks stayed at max during the timed region' if burst else 'SM clocks dropped during the timed region'}); "
-                "B200 dense tf32:bf16:int8 = 1:2:4"
-            )
-        else:
-            peak = pk["hbm_gbs"]
-            achieved = dk["work"] / (avg_ms * 1e-3) / 1e9
-            unit = "GB/s"
-            peak_note = f"{src} STREAM-style copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"
-        value = units * args.steps / (total_ms * 1e-3)
-        hbm_bytes = sum(w["work"] for w in work if w["bound"] == "hbm")
-        hbm_ms = sum(per_launch[i] for i, w in enumerate(work) if w["bound"] == "hbm") / args.steps
-        result = {
-            "metric": METRIC,
-            "value": round(value, 3),
-            "unit": wl.unit,
-            "n_gpus": n,
-            "steps": args.steps,
-            "warmup": warm,
-            "ms_per_step": round(total_ms / args.steps, 4),
-            "higher_is_better": True,
-            "scaling": scaling,
-            "vs_baseline": None,
-            "dtype": wl.dtype,
-            "data": "synthetic: seeded torch.randn inputs and random-init weights of the workload's shapes",
-            "config": {**wl.config(), "parallelism": wl.parallelism(n) if hasattr(wl, "parallelism") else f"dp{n}: " + (
-                f"{wl.global_rows // n} rows per GPU, gradients averaged by NCCL all-reduce "
-                + ("as one grouped call after the backward" if args.train_buckets == "final" else "per gradient, overlapped with the backward")
-                if args.workload == "train" else "independent row shards per GPU, no collective")},
-            "roofline": {
-                "bound": dk["bound"],
-                "kernel": dk["name"],
-                "achieved": round(achieved, 2),
-                "peak": round(peak, 1),
-                "unit": unit,
-                "frac": round(achieved / peak, 4),
-                "traffic": read_traffic(args.workload, dk["name"]),
-                "peak_source": peak_note,
-                **({"also": dk["also"]} if dk.get("also") else {}),
-            },
-            "hbm_kernels": {
-                "algorithmic_bytes_per_exec": hbm_bytes,
-                "achieved_gbs": round(hbm_bytes / (hbm_ms * 1e-3) / 1e9, 1) if hbm_ms > 0 else None,
-                "frac_of_measured_hbm": round(hbm_bytes / (hbm_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4) if hbm_ms > 0 else None,
-            },
-            "kernels": [
-                {"name": w["name"], "kind": w["kind"], "avg_ms": round(per_launch[i] / args.steps, 4), "share": round(shares[i], 4)}
-                for i, w in enumerate(work)
-            ],
-            "e2e": {
-                "value": round(units * args.steps / (e2e_ms * 1e-3), 3),
-                "unit": wl.unit,
-                "h2d_bytes_per_step": wl.h2d_bytes(),
-                "d2h_bytes_per_step": wl.d2h_bytes(),
-                "how": ("compiled.function(arena, pinned host feeds, stream) then a copy of every output to pinned host "
-                        "memory, calls alternating two streams and two arenas so copies overlap the neighbouring calls"
-                        if hasattr(wl, "run_e2e") else "one call at a time: pinned host inputs copied in, result copied out"),
-            },
-            "gpu_launches": args.steps * wl.launches_per_step(),
-            "clocks": clocks,
-        }
-        if n == 1 and not args.no_cpu_baseline:
-            result["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
+    runner = Runner(args, device, dist, n, rank, local)
+    result = measure(args.workload, runner, args.steps, args.warmup, with_cpu=(n == 1 and not args.no_cpu_baseline))
+    if not args.only:
+        nested = {}
+        for name in SUB_WORKLOADS:
+            if name == args.workload:
+                continue
+            nested[name] = measure(name, runner, args.sub_steps or args.steps, 3, with_cpu=False)
+        if result is not None:
+            result["workloads"] = nested
     if dist:
         dist.barrier()
         dist.destroy_process_group()

@@ -62,12 +62,21 @@ MACHINES = {m.name: m for m in (CPU, GPU, BANDWIDTH_STARVED)}
 TENSOR_RATE = {"tf32": 0.5, "bf16": 1.0, "int8": 2.0}
 
 
+# float32 on the CUDA cores (no tensor core): 148 SMs x 128 lanes x 2 flops per fused
+# multiply-add x 1.965 GHz; a nominal figure, not a measurement
+B200_FP32_SIMT_FLOPS = 148 * 128 * 2 * 1.965e9
+
+
 def b200(peaks: dict, kind: str = "tf32", sustained: bool = False) -> Machine:
-    """The B200 as a roofline machine: the measured copy bandwidth and the dense tensor rate of
-    ``kind`` derived from the measured bf16 GEMM rate (burst, or ``sustained`` under the power
-    cap). ``peaks`` holds ``hbm_gbs``, ``bf16_tflops`` and ``bf16_tflops_sustained``."""
+    """The B200 as a roofline machine: the measured copy bandwidth and, for ``kind`` tf32, bf16
+    or int8, the dense tensor rate derived from the measured bf16 GEMM rate (burst, or
+    ``sustained`` under the power cap); for ``kind`` fp32 the nominal CUDA-core rate (the
+    elementwise and reduction kernels). ``peaks`` holds ``hbm_gbs``, ``bf16_tflops`` and
+    ``bf16_tflops_sustained``."""
+    if kind == "fp32":
+        return Machine(B200_FP32_SIMT_FLOPS, peaks["hbm_gbs"] * 1e9, "b200-fp32")
     if kind not in TENSOR_RATE:
-        raise ConfigError(f"no B200 tensor rate for {kind!r}; expected one of {sorted(TENSOR_RATE)}")
+        raise ConfigError(f"no B200 rate for {kind!r}; expected fp32 or one of {sorted(TENSOR_RATE)}")
     bf16 = peaks["bf16_tflops_sustained" if sustained else "bf16_tflops"]
     return Machine(bf16 * 1e12 * TENSOR_RATE[kind], peaks["hbm_gbs"] * 1e9, f"b200-{kind}")
 

@@ -556,6 +556,27 @@ class Graph:
         return f"graph({header}) {{\n{body}\n  return {', '.join(self.outputs)}\n}}"
 
 
+def adopt(graph) -> Graph:
+    """``graph`` as a tgcb Graph. A tgcb Graph is returned as it is; a graph of tgc's own IR
+    (tgc/ir/graph.py:109-196: ``inputs`` of values, ``nodes`` in topological order, ``outputs``
+    by name) is rebuilt value by value, looking each operation and dtype up by its name, so
+    it prints, validates and compiles exactly like the same graph built with tgcb's Builder."""
+    if isinstance(graph, Graph):
+        return graph
+
+    def value(v) -> Value:
+        dims = tuple(Dim(d.value, d.name) for d in v.shape.sizes)
+        return Value(v.name, Shape(dims), dtype_from_name(v.dtype.name))
+
+    try:
+        inputs = [value(v) for v in graph.inputs]
+        nodes = [Node(get_op(n.op.name), tuple(n.inputs), value(n.output), dict(n.attrs)) for n in graph.nodes]
+        outputs = list(graph.outputs)
+    except AttributeError as e:
+        raise GraphError(f"not a graph: {e}") from None
+    return Graph(nodes, inputs, outputs)
+
+
 def validate(graph) -> None:
     """Topological order, single assignment, defined outputs (tgc/ir/graph.py:199-225)."""
     defined: set[str] = set()

@@ -195,7 +195,10 @@ def _operand_desc(op, lowering: Lowering, offsets: dict[str, int], tile_rows: in
 
 
 def generate(graph, *, pipeline=None, optimise: bool = True) -> tuple:
-    """Everything up to (not including) loading: (optimised graph, order, plan, module, lowering)."""
+    """Everything up to (not including) loading: (optimised graph, order, plan, module, lowering).
+
+    ``graph`` may be tgc's own Graph: it is rebuilt in tgcb's IR first (``ir.adopt``)."""
+    graph = ir.adopt(graph)
     ir.validate(graph)
     if not can_lower(graph):
         raise CodegenError("this graph has operations or shapes the backend cannot lower")

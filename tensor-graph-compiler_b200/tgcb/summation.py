@@ -16,7 +16,9 @@ are the leaves of the perfect tree that forms the top k levels (``tgcb_sum_perfe
 from __future__ import annotations
 
 import ctypes
+import math
 
+import numpy as np
 import torch
 
 from tgcb import _lib
@@ -178,3 +180,44 @@ def sequential(values: torch.Tensor) -> float:
     out = torch.empty(1, dtype=torch.float32, device=v.device)
     sequential_into(v, out)
     return float(out.item())
+
+
+def exact(values) -> float:
+    """The correctly rounded float64 value of the exact sum of float32 values (tgc's
+    summation.exact, summation.py:47-53, which rounds math.fsum's exact running sum once).
+
+    Every finite float32 is a signed integer below 2^24 times 2^(e - 150), with e its biased
+    exponent field (1 for subnormals). The integers are read from the bit patterns, summed per
+    exponent (as 12-bit halves, so the float64 sums of bincount stay exact below 2^53), and the
+    256 sums are combined as one Python integer and rounded once by integer true division. It
+    runs with torch on the tensor's own device, so a CUDA tensor is summed where it lies; arrays
+    and CPU tensors are summed on the CPU. Non-finite inputs take math.fsum's answer.
+    """
+    t = values if isinstance(values, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(values))
+    t = t.detach().reshape(-1)
+    if t.dtype != torch.float32:
+        raise ConfigError(f"these orders are about float32, got {t.dtype}")
+    if t.numel() == 0:
+        raise ConfigError("there is nothing to sum")
+    bits = t.contiguous().view(torch.int32)
+    field = (bits >> 23) & 0xFF
+    if bool((field == 0xFF).any()):
+        return math.fsum(t.cpu().double().tolist())
+    mant = bits & 0x7FFFFF
+    ints = torch.where(field > 0, mant | 0x800000, mant)
+    ints = torch.where(bits < 0, -ints, ints)
+    slot = field.clamp_min(1).long()
+    hi = torch.bincount(slot, weights=(ints >> 12).double(), minlength=256).tolist()
+    lo = torch.bincount(slot, weights=(ints & 0xFFF).double(), minlength=256).tolist()
+    total = 0
+    for k in range(256):
+        if hi[k] or lo[k]:
+            total += ((int(hi[k]) << 12) + int(lo[k])) << k
+    return total / (1 << 150)
+
+
+def relative_error(approximate: float, reference: float) -> float:
+    """|approximate - reference| / |reference| (tgc's summation.relative_error, summation.py:134-139)."""
+    if reference == 0.0:
+        raise ConfigError("a relative error against zero is undefined")
+    return abs(approximate - reference) / abs(reference)

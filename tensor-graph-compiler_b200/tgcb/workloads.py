@@ -33,6 +33,14 @@ def cone_graph(B, rows: int = 4096, cols: int = 1024):
     return b.finish(b.sum(t, [1]), b.max(t, [1]), b.sum(b.mul(t, x), [1]))
 
 
+def row_sum_graph(B, rows: int = 4096, cols: int = 1024):
+    """The cone's input read once and summed per row, nothing else: the same row kernel launch
+    shape as the cone with no arithmetic to hide, the ceiling a launch over these bytes reaches."""
+    b = B()
+    x = b.input([rows, cols], name="x")
+    return b.finish(b.sum(x, [1]))
+
+
 def _gelu_tanh(b, h):
     k = b.constant(GELU_K)
     c = b.constant(GELU_C)

@@ -1,7 +1,7 @@
 """Golden outputs of tgc's attention and normalisation analyses, made by running tgc itself.
 Run once where tgc's source tree is available (it is not on the GPU hosts):
 
-    PYTHONPATH=/root/reference python tests/golden/make_analysis_golden.py
+    TGC_REFERENCE=<path to tgc's source tree> python tests/golden/make_analysis_golden.py
 
 Writes analysis.npz: tgc.analysis.attention.streaming_attention / naive_attention on
 random_head inputs, and tgc.analysis.normalisation layer_norm / rms_norm / batch_norm on
@@ -17,7 +17,9 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, os.environ.get("TGC_REFERENCE", "/root/reference"))
+if not os.environ.get("TGC_REFERENCE"):
+    sys.exit("set TGC_REFERENCE to the root of tgc's source tree")
+sys.path.insert(0, os.environ["TGC_REFERENCE"])
 
 from tgc.analysis import attention as A  # noqa: E402
 from tgc.analysis import normalisation as N  # noqa: E402

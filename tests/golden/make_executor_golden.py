@@ -1,7 +1,7 @@
 """Graphs of tgc's executor tests, printed by tgc itself. Run once where tgc's source tree is
 available (it is not on the GPU hosts):
 
-    PYTHONPATH=/root/reference python tests/golden/make_executor_golden.py
+    TGC_REFERENCE=<path to tgc's source tree> python tests/golden/make_executor_golden.py
 
 Writes graphs/exec_<name>.tgc for the graphs tgc's tests/test_executor.py runs through
 compile_graph (its GRAPHS table, plus the transpose pair and chain of tgc/passes/layout.py).
@@ -13,7 +13,9 @@ import os
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, os.environ.get("TGC_REFERENCE", "/root/reference"))
+if not os.environ.get("TGC_REFERENCE"):
+    sys.exit("set TGC_REFERENCE to the root of tgc's source tree")
+sys.path.insert(0, os.environ["TGC_REFERENCE"])
 
 from tgc.ir.builder import branching_graph, diamond_graph, elementwise_chain, layernorm_graph, mlp_graph, softmax_graph  # noqa: E402
 from tgc.ir.serialize import dumps  # noqa: E402

@@ -1,7 +1,7 @@
 """Golden fixtures for the graph fuzzer, made by running tgc's own generator and interpreter.
 Run once where tgc's source tree is available (it is not on the GPU hosts):
 
-    PYTHONPATH=/root/reference python tests/golden/make_fuzz_golden.py
+    TGC_REFERENCE=<path to tgc's source tree> python tests/golden/make_fuzz_golden.py
 
 Writes
   fuzz.json   for each generator configuration, tgc.verify.fuzz.generate(config, seed) printed
@@ -20,7 +20,9 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REFERENCE = os.environ.get("TGC_REFERENCE", "/root/reference")
+REFERENCE = os.environ.get("TGC_REFERENCE")
+if not REFERENCE:
+    sys.exit("set TGC_REFERENCE to the root of tgc's source tree")
 sys.path.insert(0, REFERENCE)
 
 from tgc.ir.serialize import dumps  # noqa: E402

@@ -1,7 +1,7 @@
 """Generate the golden fixtures by running tgc itself. Run once, where tgc's source tree is
 available (it is not on the GPU hosts); the outputs are committed next to this script.
 
-    PYTHONPATH=/root/reference python tests/golden/make_golden.py
+    TGC_REFERENCE=<path to tgc's source tree> python tests/golden/make_golden.py
 
 What it writes (all from tgc's own code paths on seeded inputs):
   graphs/*.tgc          tgc.ir.serialize.dumps of every workload graph, built with tgc's
@@ -36,7 +36,9 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(REPO, "tensor-graph-compiler_b200"))
-REFERENCE = os.environ.get("TGC_REFERENCE", "/root/reference")
+REFERENCE = os.environ.get("TGC_REFERENCE")
+if not REFERENCE:
+    sys.exit("set TGC_REFERENCE to the root of tgc's source tree")
 sys.path.insert(0, REFERENCE)
 
 from tgc.analysis import quantize as tq  # noqa: E402

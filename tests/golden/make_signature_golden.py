@@ -1,7 +1,7 @@
 """Golden shape signatures, made by running tgc's own hash. Run once where tgc's source tree
 is available (it is not on the GPU hosts):
 
-    PYTHONPATH=/root/reference python tests/golden/make_signature_golden.py
+    TGC_REFERENCE=<path to tgc's source tree> python tests/golden/make_signature_golden.py
 
 Writes signatures.json: tgc.runtime.cache.shape_signature of every graph under graphs/ and of
 the fuzz graphs in fuzz.json (loaded with tgc.ir.serialize.loads), and of tgc's
@@ -15,7 +15,9 @@ import os
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, os.environ.get("TGC_REFERENCE", "/root/reference"))
+if not os.environ.get("TGC_REFERENCE"):
+    sys.exit("set TGC_REFERENCE to the root of tgc's source tree")
+sys.path.insert(0, os.environ["TGC_REFERENCE"])
 
 from tgc.ir.isomorphism import renamed  # noqa: E402
 from tgc.ir.serialize import loads  # noqa: E402

@@ -35,6 +35,24 @@ def test_single_rank_step_matches_oracle(cuda):
         assert rel_err(g, r) < TF32_TOL
 
 
+@pytest.mark.parametrize("rows", [8192, 65536])
+def test_full_size_step_matches_oracle(cuda, rows):
+    """The training step at the sizes the benchmark runs: one 8192-row shard (8 GPUs) and the
+    whole 65536-row batch on one GPU, d 1024, f 4096, compiled exactly as the benchmark compiles
+    it (GEMM chains, row prologues and the split rules on), all four gradients against the
+    oracle's whole-graph interpreter within 5e-3 of each gradient's largest entry."""
+    feeds = workloads.mlp_inputs(rows=rows, target=True)
+    step = parallel.DataParallelTrainStep(rows, 1, 0)
+    grads = step.step({k: v.cuda() for k, v in feeds.items()})
+    torch.cuda.synchronize()
+    step.compiled.check_status()
+    torch.set_num_threads(os.cpu_count() or 1)
+    ref = interp.run(step.graph, feeds)
+    for g, r in zip(grads, ref, strict=True):
+        assert g.shape == r.shape
+        assert rel_err(g, r) < TF32_TOL
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
