@@ -329,6 +329,113 @@ __global__ void sequential_chain(const float* __restrict__ x, long long n, float
   *out = t;
 }
 
+// The sequential order for long vectors: the chain of n dependent additions runs at the adder's
+// latency only if the next values are always at hand, which one thread's own loads cannot
+// arrange (a few hundred bytes in flight against the memory latency). So one block of two
+// working threads splits the work: thread 32 streams the 16-byte-aligned body of x into a ring
+// of shared-memory slots with bulk copies (cp.async.bulk, no multicast), up to
+// kSeqSlots * kSeqChunk bytes in flight; thread 0 adds every value from 0.0f in index order,
+// reading head, slots and tail in turn, so the additions are exactly summation.sequential's.
+// Every wait is bounded; a consumer that gives up writes NaN, and the producer then waits
+// (bounded) for its copies in flight before the block exits.
+constexpr int kSeqChunk = 8192;   // bytes per slot and per bulk copy
+constexpr int kSeqSlots = 16;     // 128 KiB of shared memory
+constexpr unsigned kSeqPolls = 1u << 24;
+constexpr int kSeqSmem = kSeqSlots * kSeqChunk + 2 * kSeqSlots * 8;
+
+__device__ __forceinline__ bool seq_wait(uint32_t bar, uint32_t parity) {
+  for (unsigned i = 0; i < kSeqPolls; ++i) {
+    uint32_t ok;
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+__global__ void __launch_bounds__(64) sequential_staged(const float* __restrict__ x, long long n, float* __restrict__ out) {
+  extern __shared__ __align__(128) unsigned char seq_smem[];
+  __shared__ volatile int abort_flag;
+  __shared__ volatile long long consumed;
+  unsigned long long* bars = reinterpret_cast<unsigned long long*>(seq_smem + kSeqSlots * kSeqChunk);
+  const uint32_t ring = static_cast<uint32_t>(__cvta_generic_to_shared(seq_smem));
+  const uint32_t bar0 = static_cast<uint32_t>(__cvta_generic_to_shared(bars));  // full[s], then empty[s]
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(x);
+  long long head = (long long)(((16u - (addr & 15u)) & 15u) / 4u);  // floats before the first 16-byte boundary
+  if (head > n) head = n;
+  const long long body = ((n - head) / 4) * 4;  // whole 16-byte units
+  const long long body_bytes = body * 4;
+  const long long chunks = (body_bytes + kSeqChunk - 1) / kSeqChunk;
+  if (threadIdx.x == 0) {
+    for (int q = 0; q < 2 * kSeqSlots; ++q)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8u * q));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    abort_flag = 0;
+    consumed = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 32) {
+    long long issued = 0;
+    for (long long c = 0; c < chunks; ++c) {
+      const int slot = (int)(c % kSeqSlots);
+      const long long round = c / kSeqSlots;
+      if (round > 0 && !seq_wait(bar0 + 8u * (kSeqSlots + slot), (uint32_t)((round - 1) & 1))) break;
+      if (abort_flag) break;
+      const long long off = c * kSeqChunk;
+      const uint32_t bytes = (uint32_t)(body_bytes - off < kSeqChunk ? body_bytes - off : kSeqChunk);
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar0 + 8u * slot), "r"(bytes) : "memory");
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       ring + slot * kSeqChunk),
+                   "l"(reinterpret_cast<const char*>(x + head) + off), "r"(bytes), "r"(bar0 + 8u * slot)
+                   : "memory");
+      issued = c + 1;
+    }
+    if (abort_flag) {
+      // the consumer gave up: let the copies still in flight land before the block exits
+      for (long long c = consumed; c < issued; ++c)
+        seq_wait(bar0 + 8u * (int)(c % kSeqSlots), (uint32_t)((c / kSeqSlots) & 1));
+    }
+  } else if (threadIdx.x == 0) {
+    float t = 0.0f;
+    for (long long i = 0; i < head; ++i) t = __fadd_rn(t, __ldg(x + i));
+    for (long long c = 0; c < chunks; ++c) {
+      const int slot = (int)(c % kSeqSlots);
+      if (!seq_wait(bar0 + 8u * slot, (uint32_t)((c / kSeqSlots) & 1))) {
+        abort_flag = 1;
+        *out = __int_as_float(0x7fc00000);
+        return;
+      }
+      const long long off = c * kSeqChunk;
+      const int nv = (int)((body_bytes - off < kSeqChunk ? body_bytes - off : kSeqChunk) / 16);
+      const float4* p = reinterpret_cast<const float4*>(seq_smem + slot * kSeqChunk);
+      int q = 0;
+      for (; q + 8 <= nv; q += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = p[q + j];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          t = __fadd_rn(t, v[j].x);
+          t = __fadd_rn(t, v[j].y);
+          t = __fadd_rn(t, v[j].z);
+          t = __fadd_rn(t, v[j].w);
+        }
+      }
+      for (; q < nv; ++q) {
+        const float4 v = p[q];
+        t = __fadd_rn(t, v.x);
+        t = __fadd_rn(t, v.y);
+        t = __fadd_rn(t, v.z);
+        t = __fadd_rn(t, v.w);
+      }
+      consumed = c + 1;
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar0 + 8u * (kSeqSlots + slot)) : "memory");
+    }
+    for (long long i = head + body; i < n; ++i) t = __fadd_rn(t, __ldg(x + i));
+    *out = t;
+  }
+}
+
 // One CTA per row. The row stays in registers between the max pass and the quantise pass.
 template <int PER_THREAD>
 __global__ void __launch_bounds__(256) quantise_rows(const float* __restrict__ x, long long rows, long long cols,
@@ -560,9 +667,18 @@ int tgcb_sum_perfect_tree_f32(const float* partials, uint32_t count, float* out,
 int tgcb_sum_sequential_f32(const float* x, uint64_t n, float* out, void* stream) {
   if (x == nullptr || out == nullptr) return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_sequential_f32", "null pointer");
   if (n == 0) return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_sum_sequential_f32", "there is nothing to sum");
-  sequential_chain<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(x, (long long)n, out);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return report(TGCB_E_CUDA, "sequential_chain", e);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n < (1u << 16)) {
+    sequential_chain<<<1, 32, 0, s>>>(x, (long long)n, out);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return report(TGCB_E_CUDA, "sequential_chain", e);
+    return TGCB_OK;
+  }
+  cudaError_t e = cudaFuncSetAttribute(sequential_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, kSeqSmem);
+  if (e != cudaSuccess) return report(TGCB_E_CUDA, "sequential_staged shared memory", e);
+  sequential_staged<<<1, 64, kSeqSmem, s>>>(x, (long long)n, out);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return report(TGCB_E_CUDA, "sequential_staged", e);
   return TGCB_OK;
 }
 

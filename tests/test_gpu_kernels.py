@@ -99,10 +99,22 @@ def test_pairwise_any_length_any_block(cuda, n, block):
     assert summation.pairwise(v.cuda(), block) == bracketing.pairwise(v.numpy(), block)
 
 
-@pytest.mark.parametrize("n", [1, 5, 1000, 65537])
+@pytest.mark.parametrize("n", [1, 5, 1000, 65535, 65537, 2048 * 16 * 3 + 7])
 def test_sequential_any_length(cuda, n):
     v = torch.rand(n, generator=torch.Generator().manual_seed(n))
     assert summation.sequential(v.cuda()) == bracketing.sequential(v.numpy())
+
+
+@pytest.mark.parametrize("offset", [1, 2, 3])
+@pytest.mark.parametrize("n", [70001, (1 << 20) + 5])
+def test_sequential_on_unaligned_views(cuda, n, offset):
+    """Long vectors stream through shared memory in 16-byte-aligned bulk copies; a view that
+    starts 4, 8 or 12 bytes past a 16-byte boundary adds its head and ragged tail directly, in
+    the same left-to-right order."""
+    v = torch.rand(n, generator=torch.Generator().manual_seed(n + offset)) - 0.25
+    vc = v.cuda()[offset:]
+    assert vc.data_ptr() % 16 != 0
+    assert summation.sequential(vc) == bracketing.sequential(v.numpy()[offset:])
 
 
 @pytest.mark.parametrize("n", [4099, (1 << 20) + 3])
