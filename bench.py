@@ -58,7 +58,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["tgcb", "reference"], default="tgcb")
-    p.add_argument("--workload", choices=["mlp", "cone", "int8", "longsum", "train"], default="mlp")
+    p.add_argument("--workload", choices=["mlp", "cone", "int8", "longsum", "train", "attention"], default="mlp")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--only", action="store_true", help="time the chosen workload alone, without the others under 'workloads'")
@@ -740,7 +740,7 @@ class LongSumWorkload:
                 "ms": round(seq_ms, 3),
                 "gbs": round(self.n * 4 / (seq_ms * 1e-3) / 1e9, 2),
                 "bound": "latency: one chain of 2^26 dependent float adds on one thread",
-                "kernel": "sequential_chain",
+                "kernel": "sequential_staged",
             },
             "error_vs_fp64": {
                 "vector": "rank 0's 2^26 values (the long-sum workload's seed-0 input)",
@@ -938,10 +938,86 @@ class TrainWorkload:
         return lambda _feeds: prog(feeds)
 
 
+class AttentionWorkload:
+    """One head of streaming attention (tgc/analysis/attention.py:97-137): 8192 queries against
+    8192 keys and values of width 64, float32, one fused kernel (tgcb.attention). Both products
+    run on the CUDA cores in float32, as tgc's float32 matmuls do; the roofline is the CUDA
+    cores' nominal float32 rate. One unit is one head; per GPU fixed ("weak")."""
+
+    name = "attention"
+    unit = "heads/s"
+    dtype = "f32"
+    seq, width = 8192, 64
+
+    def __init__(self, rank: int):
+        self.rank = rank
+
+    def config(self):
+        return {"workload": f"streaming attention, one head: q, k, v [{self.seq},{self.width}] fp32 ~N(0,1); "
+                            "softmax(q k^T / sqrt(64)) v in one pass over the keys",
+                "flops_per_head": 4 * self.seq * self.seq * self.width, "l2": L2_NOTE}
+
+    def setup(self, device):
+        import torch
+
+        g = torch.Generator().manual_seed(self.rank)
+        self.host = [torch.randn(self.seq, self.width, generator=g).pin_memory() for _ in range(3)]
+        self.dev = [t.to(device) for t in self.host]
+        self.out = torch.empty_like(self.dev[0])
+        self.staging = [torch.empty_like(t) for t in self.dev]
+        self.out_host = torch.empty(self.seq, self.width).pin_memory()
+
+    def launches_per_step(self) -> int:
+        return 1
+
+    def step_profiled(self) -> list[float]:
+        import torch
+
+        from tgcb import attention
+
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        attention.streaming_attention_into(*self.dev, self.out)
+        e.record()
+        e.synchronize()
+        return [s.elapsed_time(e)]
+
+    def step_e2e(self) -> None:
+        from tgcb import attention
+
+        for d, h in zip(self.staging, self.host, strict=True):
+            d.copy_(h, non_blocking=True)
+        attention.streaming_attention_into(*self.staging, self.out)
+        self.out_host.copy_(self.out, non_blocking=True)
+
+    def h2d_bytes(self) -> int:
+        return 3 * self.seq * self.width * 4
+
+    def d2h_bytes(self) -> int:
+        return self.seq * self.width * 4
+
+    def kernel_work(self) -> list[dict]:
+        return [{"name": "streaming_attention<64>", "kind": "attention", "bound": "fp32", "work": 4 * self.seq * self.seq * self.width}]
+
+    @property
+    def cpu_feeds(self):
+        return {}
+
+    def cpu_program(self):
+        """tgc's streaming_attention restated by the oracle (torch CPU, float32, blocks of 128)."""
+        import torch
+
+        from oracle import analysis
+
+        g = torch.Generator().manual_seed(self.rank)
+        q, k, v = (torch.randn(self.seq, self.width, generator=g) for _ in range(3))
+        return lambda _feeds: analysis.streaming_attention(q, k, v)
+
+
 WORKLOADS = {"mlp": MlpWorkload, "cone": ConeWorkload, "int8": Int8Workload, "longsum": LongSumWorkload,
-             "train": TrainWorkload}
+             "train": TrainWorkload, "attention": AttentionWorkload}
 # timed after the headline workload in the same run, each reported under "workloads"
-SUB_WORKLOADS = ("cone", "longsum", "int8", "train")
+SUB_WORKLOADS = ("cone", "longsum", "int8", "train", "attention")
 
 
 # ----------------------------------------------------------------------------- cpu baseline
@@ -1102,6 +1178,14 @@ def roofline_of(wl, runner: Runner, per_launch: list[float], steps: int, clocks:
             f"{'SM clocks stayed at max during the timed region' if burst else 'SM clocks dropped during the timed region'}); "
             "B200 dense tf32:bf16:int8 = 1:2:4"
         )
+    elif dk["bound"] == "fp32":
+        from tgcb import cost
+
+        peak = cost.B200_FP32_SIMT_FLOPS / 1e12
+        achieved = dk["work"] / (avg_ms * 1e-3) / 1e12
+        unit = "TFLOP/s"
+        peak_note = ("nominal float32 CUDA-core rate (148 SMs x 128 lanes x 2 flops per FMA x 1.965 GHz); no measured "
+                     "float32 peak exists in MEASURED_PEAKS.json, so this fraction is of nominal")
     else:
         peak = pk["hbm_gbs"]
         achieved = dk["work"] / (avg_ms * 1e-3) / 1e9

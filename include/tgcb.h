@@ -56,7 +56,10 @@ typedef struct tgcb_operand_desc {
   uint32_t box_cols;     /* TMA box extent along the contiguous axis (elements) */
   uint32_t box_rows;     /* TMA box extent along rows */
   uint32_t swizzle;      /* 0: 128-byte swizzle of 16-byte units; 1: of 32-byte units (tf32 MN-major) */
-  uint32_t reserved;
+  uint32_t chunks;       /* 0: a 2-D map of boxes box_cols x box_rows. c > 0 (swizzle 1, cols a multiple
+                            of 32): a 3-D view (32 columns, rows, cols / 32 chunks) whose box takes c
+                            chunks of 32 columns x box_rows rows at once, laid out chunk after chunk:
+                            one copy of box_rows x 32c values instead of c copies of 4 KB */
 } tgcb_operand_desc;
 
 /* One kernel launch of a plan. Plain kernels take TgcbArgs; GEMM kernels take TgcbArgs

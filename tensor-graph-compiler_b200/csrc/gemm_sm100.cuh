@@ -99,6 +99,29 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const TgcbTmaDesc* des
       : "memory");
 }
 
+// The same through a 3-D view (x within a 32-column chunk, y = row, z = chunk): one copy of
+// several 32-column chunks, which the 2-D form needs one 4 KB copy each for.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const TgcbTmaDesc* desc, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<unsigned long long>(desc)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+// Whether an MN-major operand is loaded through the 3-D view (the runtime encodes that view for
+// the same operands: tgcb_operand_desc.chunks > 0). tf32 MN-major stages are 32-column chunks of
+// 4 KB; tiled copies that small fill shared memory at well under half the rate of 16 KB ones,
+// so a whole stage of chunks is one copy when the MN extent is a multiple of 32. int8 MN-major
+// stages are 16 KB boxes already.
+// TGCB_CHUNKED_MN (set by the generated source, default 1) turns the 3-D form off for
+// comparisons.
+#ifndef TGCB_CHUNKED_MN
+#define TGCB_CHUNKED_MN 1
+#endif
+__host__ __device__ constexpr bool chunked_mn(bool int8, bool mn_major, int mn_extent) {
+  return TGCB_CHUNKED_MN && !int8 && mn_major && mn_extent % 32 == 0;
+}
+
 // Shared-memory matrix descriptor with sm_100 version bits. layout 2 = 128-byte swizzle in
 // 16-byte units (8-row atoms); layout 1 = 128-byte swizzle in 32-byte units (4-row atoms),
 // the only layout tcgen05 accepts for MN-major 32-bit (tf32) operands.
@@ -230,6 +253,8 @@ __device__ __forceinline__ void gemm_body(const TgcbArgs& args, const TgcbTmaDes
           const uint32_t b_dst = sB + stage * B_STAGE;
           if (!A_MN) {
             tma_load_2d(a_dst, ta, kb * KB, tm * BM, full_bar(stage));
+          } else if constexpr (chunked_mn(INT8, A_MN, M)) {
+            tma_load_3d(a_dst, ta, 0, kb * KB, tm * BM / 32, full_bar(stage));
           } else {
 #pragma unroll
             for (int c = 0; c < BM * EB / ROW_BYTES; ++c)
@@ -237,6 +262,8 @@ __device__ __forceinline__ void gemm_body(const TgcbArgs& args, const TgcbTmaDes
           }
           if (!B_MN) {
             tma_load_2d(b_dst, tb, kb * KB, tn * BN, full_bar(stage));
+          } else if constexpr (chunked_mn(INT8, B_MN, N)) {
+            tma_load_3d(b_dst, tb, 0, kb * KB, tn * BN / 32, full_bar(stage));
           } else {
 #pragma unroll
             for (int c = 0; c < BN * EB / ROW_BYTES; ++c)

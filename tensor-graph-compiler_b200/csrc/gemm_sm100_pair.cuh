@@ -21,7 +21,10 @@
 
 namespace tgcb_gemm {
 
-constexpr int P_STAGES = 6;
+#ifndef TGCB_PAIR_STAGES
+#define TGCB_PAIR_STAGES 6
+#endif
+constexpr int P_STAGES = TGCB_PAIR_STAGES;
 constexpr int P_A_STAGE = BM * ROW_BYTES;         // 16 KB: this CTA's 128 rows of A
 constexpr int P_B_STAGE = (BN / 2) * ROW_BYTES;   // 16 KB: this CTA's 128 columns of B
 constexpr int P_SMEM_BYTES = P_STAGES * (P_A_STAGE + P_B_STAGE) + BAR_BYTES + EPI_STAGE_BYTES + 1024;
@@ -69,6 +72,13 @@ __device__ __forceinline__ void mma_pair(uint32_t d_tmem, unsigned long long a, 
         "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8, %5, %6, %7, %8}, p; }" ::"r"(d_tmem),
         "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
   }
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const TgcbTmaDesc* desc, int x, int y, int z, uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<unsigned long long>(desc)), "r"(x), "r"(y), "r"(z), "r"(cluster_bar)
+      : "memory");
 }
 
 // Arrive on a barrier (this CTA's or the peer's) when every MMA issued so far has completed.
@@ -179,6 +189,8 @@ __device__ __forceinline__ bool produce_tile(const PairCta& c, const TgcbArgs& a
     const uint32_t b_dst = c.sB + r.stage * P_B_STAGE;
     if (!G::A_MN) {
       tma_load_2d_pair(a_dst, ta, kb * KB, arow, lead_full);
+    } else if constexpr (chunked_mn(INT8, G::A_MN, G::M)) {
+      tma_load_3d_pair(a_dst, ta, 0, kb * KB, arow / 32, lead_full);
     } else {
 #pragma unroll
       for (int q = 0; q < BM * EB / ROW_BYTES; ++q)
@@ -186,6 +198,8 @@ __device__ __forceinline__ bool produce_tile(const PairCta& c, const TgcbArgs& a
     }
     if (!G::B_MN) {
       tma_load_2d_pair(b_dst, tb, kb * KB, bcol, lead_full);
+    } else if constexpr (chunked_mn(INT8, G::B_MN, G::N)) {
+      tma_load_3d_pair(b_dst, tb, 0, kb * KB, bcol / 32, lead_full);
     } else {
 #pragma unroll
       for (int q = 0; q < (BN / 2) * EB / ROW_BYTES; ++q)

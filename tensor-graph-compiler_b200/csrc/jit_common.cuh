@@ -43,17 +43,20 @@ struct TgcbArgs {
 #endif
 
 // Approximate functions for TF32 GEMM epilogues only, whose results are compared at TF32
-// tolerance; every other kernel calls CUDA's accurate functions. tanh(u) = 1 - 2 / (1 + e^(2u))
-// and sigmoid(u) = 1 / (1 + e^(-u)) from the hardware exponential and the hardware reciprocal
-// (PTX rcp.approx, about 1 ulp; its argument 1 + e^x is never below 1, and 1/inf is 0):
-// absolute error ~1e-6 or less over the whole range, +-1 and 0/1 at the ends.
-__device__ __forceinline__ float tgcb_rcp_approx(float x) {
+// tolerance; every other kernel calls CUDA's accurate functions. tanh is the hardware's own
+// (PTX tanh.approx.f32: one special-function instruction, maximum relative error about 2^-11,
+// the size of one TF32 rounding of an input), and sigmoid(u) = 0.5 + 0.5 tanh(u / 2) takes the
+// same instruction. On the MLP block's GELU epilogue the first GEMM runs 6% faster with it than
+// with tanh built from the hardware exponential and reciprocal (two such instructions and more
+// arithmetic per element, in warps that share issue slots with the MMA and TMA warps), and the
+// block's largest error against the oracle is unchanged (TF32 rounding of the operands
+// dominates).
+__device__ __forceinline__ float tgcb_tanh_approx(float u) {
   float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  asm("tanh.approx.f32 %0, %1;" : "=f"(r) : "f"(u));
   return r;
 }
-__device__ __forceinline__ float tgcb_tanh_approx(float u) { return 1.0f - 2.0f * tgcb_rcp_approx(1.0f + __expf(2.0f * u)); }
-__device__ __forceinline__ float tgcb_sigmoid_approx(float u) { return tgcb_rcp_approx(1.0f + __expf(-u)); }
+__device__ __forceinline__ float tgcb_sigmoid_approx(float u) { return 0.5f + 0.5f * tgcb_tanh_approx(0.5f * u); }
 
 __device__ __forceinline__ long long tgcb_min_ll(long long a, long long b) { return a < b ? a : b; }
 __device__ __forceinline__ long long tgcb_max_ll(long long a, long long b) { return a > b ? a : b; }

@@ -308,15 +308,28 @@ static int encode_operand(DeviceState* st, const tgcb_operand_desc& od, const vo
   if ((od.cols * od.elem_bytes) % 16 != 0)
     return fail(TGCB_E_INVALID, "GEMM operand row pitch %llu bytes is not a multiple of 16",
                 (unsigned long long)(od.cols * od.elem_bytes));
-  cuuint64_t dims[2] = {od.cols, od.rows};
-  cuuint64_t strides[1] = {od.cols * od.elem_bytes};
-  cuuint32_t box[2] = {od.box_cols, od.box_rows};
-  cuuint32_t estr[2] = {1, 1};
   CUtensorMapDataType dt = od.elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const CUtensorMapSwizzle sw = od.swizzle == 1 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
-  CUresult r = st->encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r;
+  if (od.chunks > 0) {
+    // 3-D view of the row-major matrix: element (row, 32 q + j) at (j, row, q); one box covers
+    // `chunks` consecutive 32-column chunks of box_rows rows, chunk after chunk in shared memory
+    if (od.swizzle != 1 || od.elem_bytes != 4 || od.cols % 32 != 0 || od.box_cols != 32 || od.chunks > 8)
+      return fail(TGCB_E_INVALID, "a chunked (3-D) operand map needs tf32, the 32-byte-unit swizzle and 32-column chunks");
+    cuuint64_t dims[3] = {32, od.rows, od.cols / 32};
+    cuuint64_t strides[2] = {od.cols * od.elem_bytes, 32 * od.elem_bytes};
+    cuuint32_t box[3] = {32, od.box_rows, od.chunks};
+    cuuint32_t estr[3] = {1, 1, 1};
+    r = st->encode(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[2] = {od.cols, od.rows};
+    cuuint64_t strides[1] = {od.cols * od.elem_bytes};
+    cuuint32_t box[2] = {od.box_cols, od.box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    r = st->encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (r != CUDA_SUCCESS) return fail(TGCB_E_CUDA, "cuTensorMapEncodeTiled failed with %d", (int)r);
   return TGCB_OK;
 }

@@ -36,7 +36,7 @@ class OperandDesc(ctypes.Structure):
         ("box_cols", ctypes.c_uint32),
         ("box_rows", ctypes.c_uint32),
         ("swizzle", ctypes.c_uint32),
-        ("reserved", ctypes.c_uint32),
+        ("chunks", ctypes.c_uint32),
     ]
 
 

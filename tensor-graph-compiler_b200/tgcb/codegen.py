@@ -52,6 +52,7 @@ ROW_PROLOGUE = True  # a one-warp-per-row step producing a chain's first A opera
 ROW_PROLOGUE_MAX_ROUNDS = 4
 CHAIN_MAX_ITEMS = 32768  # tiles of both GEMMs together (the schedule is a __constant__ table)
 K_SPLIT = True  # an SM-pair GEMM with fewer output tiles than pairs cuts K into slices
+CHUNKED_MN = True  # tf32 MN-major operands load a stage of 32-column chunks as one 3-D copy
 SPLIT_MAX = 8
 SPLIT_MIN_KBLOCKS = 16
 _LOAD_LINE = re.compile(r"^\s*const (.+?) (ld_\d+) = (.*);$")

@@ -29,9 +29,11 @@ ELEMENTWISE_BINARY = ("add", "sub", "mul", "maximum", "minimum")
 DEFAULT_TOLERANCE = 1e-5
 
 
-@dataclass
+@dataclass(frozen=True)
 class GeneratorConfig:
-    """How large and how strange the generated graphs are (fuzz.py:37-64)."""
+    """The generator's knobs, under the names tgc's fuzzer takes them (fuzz.py:37-64): graph
+    size (nodes drawn, inputs declared), the [rows, columns] every full value has, and the
+    odds of drawing a row reduction and of reusing one operand for both sides of a binary op."""
 
     nodes: int = 12
     inputs: int = 2
@@ -41,22 +43,15 @@ class GeneratorConfig:
     reuse_chance: float = 0.3
 
     def __post_init__(self) -> None:
-        if self.nodes < 1:
-            raise ConfigError(f"a graph needs at least one node, got {self.nodes}")
-        if self.inputs < 1:
-            raise ConfigError(f"a graph needs at least one input, got {self.inputs}")
-        if not 0.0 <= self.reduction_chance <= 1.0:
-            raise ConfigError("the reduction chance has to be a probability")
-        if not 0.0 <= self.reuse_chance <= 1.0:
-            raise ConfigError("the reuse chance has to be a probability")
+        bad = [f"{k}={getattr(self, k)} (at least 1)" for k in ("nodes", "inputs") if getattr(self, k) < 1]
+        bad += [f"{k}={getattr(self, k)} (a probability, 0 to 1)" for k in ("reduction_chance", "reuse_chance")
+                if not 0.0 <= getattr(self, k) <= 1.0]
+        if bad:
+            raise ConfigError("unusable generator settings: " + ", ".join(bad))
 
     def as_dict(self) -> dict:
-        return {
-            "nodes": self.nodes,
-            "inputs": self.inputs,
-            "shape": [self.rows, self.columns],
-            "reduction_chance": self.reduction_chance,
-        }
+        return {"nodes": self.nodes, "inputs": self.inputs, "shape": [self.rows, self.columns],
+                "reduction_chance": self.reduction_chance}
 
 
 def generate(config: GeneratorConfig | None = None, seed: int = 0) -> ir.Graph:
@@ -118,18 +113,17 @@ def outputs_agree(left, right, *, tolerance: float = 0.0) -> bool:
     return True
 
 
-@dataclass
+@dataclass(frozen=True)
 class Failure:
+    """A generated graph the backend got wrong: the seed that drew it, the graph (shrunk, when
+    shrinking ran) and what went wrong."""
+
     seed: int
     graph: ir.Graph
     detail: str = ""
 
-    @property
-    def size(self) -> int:
-        return len(self.graph.nodes)
-
     def as_dict(self) -> dict:
-        return {"seed": self.seed, "nodes": self.size, "detail": self.detail}
+        return {"seed": self.seed, "nodes": len(self.graph.nodes), "detail": self.detail}
 
 
 @dataclass
@@ -150,7 +144,7 @@ class FuzzReport:
             "checked": self.checked,
             "passed": self.passed,
             "failures": len(self.failures),
-            "smallest_failure": min((f.size for f in self.failures), default=0),
+            "smallest_failure": min((len(f.graph.nodes) for f in self.failures), default=0),
         }
 
 

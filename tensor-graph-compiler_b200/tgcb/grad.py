@@ -52,26 +52,25 @@ def _sizes(shape) -> list[int]:
 
 
 def sum_to_shape(b: ir.Builder, name: str, source, target) -> str:
-    """Sum a cotangent over the axes broadcasting expanded (tgc/grad/rules.py:96-128)."""
-    src, tgt = _sizes(source), _sizes(target)
-    if src == tgt:
+    """Undo broadcasting on a cotangent: sum it over every axis that broadcasting created
+    (leading axes the operand lacks) or widened (the operand's size-1 axes), in increasing axis
+    order with the dimensions kept, then drop the leading ones with a reshape. These are the
+    builder calls tgc/grad/rules.py:96-128 makes, so gradient graphs print alike."""
+    have, want = _sizes(source), _sizes(target)
+    if have == want:
         return name
-    extra = len(src) - len(tgt)
-    if extra < 0:
-        raise PassError(f"a cotangent of rank {len(src)} cannot fit rank {len(tgt)}")
-    axes = list(range(extra))
-    aligned = tgt if extra == 0 else [1] * extra + tgt
-    for pos, (have, want) in enumerate(zip(src, aligned, strict=True)):
-        if pos < extra:
-            continue
-        if want == 1 and have != 1:
-            axes.append(pos)
-        elif want != have:
-            raise PassError(f"a cotangent of {src} does not reduce to {tgt}")
-    reduced = b.sum(name, axes=axes, keepdims=True) if axes else name
-    if _sizes(b.shape_of(reduced)) == tgt:
-        return reduced
-    return b.reshape(reduced, tgt)
+    lead = len(have) - len(want)
+    if lead < 0:
+        raise PassError(f"cannot reduce a rank-{len(have)} cotangent to rank {len(want)}")
+    padded = [1] * lead + list(want)
+    axes = []
+    for axis, (h, w) in enumerate(zip(have, padded, strict=True)):
+        if axis < lead or (w == 1 and h != 1):
+            axes.append(axis)
+        elif w != h:
+            raise PassError(f"shape {have} was not broadcast from {want}")
+    out = b.sum(name, axes=axes, keepdims=True) if axes else name
+    return out if _sizes(b.shape_of(out)) == want else b.reshape(out, want)
 
 
 def _binary_sum(b, ctx, left, right):

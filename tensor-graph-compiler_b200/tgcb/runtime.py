@@ -29,7 +29,7 @@ import re
 from collections.abc import Callable
 from dataclasses import dataclass, field
 
-from tgcb import _lib, ir, memory
+from tgcb import _lib, codegen, ir, memory
 from tgcb.codegen import Lowering, Step
 from tgcb.errors import CodegenError, ConfigError, DeviceError
 from tgcb.passes import default_pipeline
@@ -166,6 +166,7 @@ def _render(lowering: Lowering, steps: list[Step], offsets: dict[str, int]) -> s
 
     parts = ['#include "jit_common.cuh"']
     if any(s.kind == "gemm" for s in steps):
+        parts.insert(0, f"#define TGCB_CHUNKED_MN {1 if codegen.CHUNKED_MN else 0}")
         parts.append('#include "gemm_sm100.cuh"')
     if any(ln.pair for s in steps for ln in s.launches):
         parts.append('#include "gemm_sm100_pair.cuh"')
@@ -191,7 +192,16 @@ def _operand_desc(op, lowering: Lowering, offsets: dict[str, int], tile_rows: in
     d.box_rows = (128 // op.elem_bytes) if op.mn_major else tile_rows
     # tcgen05 reads MN-major 32-bit operands only in the 128-byte swizzle of 32-byte units.
     d.swizzle = 1 if (op.mn_major and op.elem_bytes == 4) else 0
+    # Such an operand's stage is tile_rows / 32 chunks of 32 columns (4 KB each): loaded as one
+    # copy through a 3-D view when the columns come in whole chunks (the kernels' chunked_mn).
+    d.chunks = tile_rows // 32 if chunked_mn(op) else 0
     return d
+
+
+def chunked_mn(op) -> bool:
+    """Whether the GEMM kernels load this operand through a 3-D view (tgcb_gemm::chunked_mn):
+    tf32, MN-major, and its contiguous extent (the M or N of the GEMM) a multiple of 32."""
+    return codegen.CHUNKED_MN and op.mn_major and op.elem_bytes == 4 and op.cols % 32 == 0
 
 
 def generate(graph, *, pipeline=None, optimise: bool = True) -> tuple:

@@ -218,3 +218,35 @@ def test_tf32_epilogues_approximate_int8_epilogues_exact():
     assert "__fmaf_rn" not in int8.steps[0].source and "approx" not in int8.steps[0].source
     cone = runtime.generate(workloads.cone_graph(ir.Builder))[3]
     assert "expf(" in cone.steps[0].source and "__expf" not in cone.steps[0].source
+
+
+@pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("M,N,K,kind", [(512, 512, 256, "f32"), (200, 300, 160, "f32"), (256, 96, 64, "f32"),
+                                        (8192, 4096, 1024, "f32"), (256, 512, 256, "i8")])
+def test_chunked_operand_maps_agree_with_the_kernels(ta, tb, M, N, K, kind):
+    """The runtime encodes a 3-D (chunked) tensor map for exactly the operands the GEMM kernels
+    load through one: tf32, MN-major, contiguous extent (the GEMM's M for A, N for B) a multiple
+    of 32 (tgcb_gemm::chunked_mn), with tile_rows / 32 chunks per box."""
+    import re
+
+    b = ir.Builder()
+    dt = ir.FLOAT32 if kind == "f32" else ir.INT8
+    a = b.input([K, M] if ta else [M, K], dt, name="a")
+    w = b.input([N, K] if tb else [K, N], dt, name="w")
+    if kind == "i8":
+        a, w = b.cast(a, ir.INT32), b.cast(w, ir.INT32)
+    g = b.finish(b.matmul(b.transpose(a, [1, 0]) if ta else a, b.transpose(w, [1, 0]) if tb else w))
+    _, _, _, module, _ = runtime.generate(g)
+    gemms = [d for d in module.launches if d.is_gemm]
+    if not gemms:
+        return  # the SIMT fallback (rows TMA cannot tile) has no tensor maps
+    d = gemms[0]
+    m = re.search(r"gemm_(?:body_pair|body|split_pair)<(\d+), (\d+), (\d+), (true|false), (true|false), (true|false)",
+                  module.source)
+    assert m, "one tensor-core GEMM instantiation"
+    gm, gn, _, is_int, a_mn, b_mn = m.groups()
+    for op, mn, extent, tile in ((d.a, a_mn == "true", int(gm), 128), (d.b, b_mn == "true", int(gn), 128 if d.is_gemm == 2 else 256)):
+        kernel_chunked = is_int == "false" and mn and extent % 32 == 0
+        assert (op.chunks > 0) == kernel_chunked
+        if kernel_chunked:
+            assert op.cols == extent and op.swizzle == 1 and op.chunks == tile // 32
