@@ -27,6 +27,25 @@ def test_streaming_attention(cuda, s, w, blk, seed, scale):
     assert float((got - ref).abs().max()) <= 2e-5 * float(ref.abs().max())
 
 
+@pytest.mark.parametrize("s,sk,w", [(1000, 777, 64), (96, 4099, 128), (33, 65, 64)])
+def test_vector_attention_kernel_equals_the_scalar_one(cuda, s, sk, w):
+    """Widths 64 and 128 run the 16-byte-operand kernel; an output buffer that is not 16-byte
+    aligned takes the scalar kernel instead. Both add in the same order, so they agree bit for
+    bit."""
+    g = torch.Generator().manual_seed(s + sk)
+    q, k, v = (torch.randn(n, w, generator=g).cuda() for n in (s, sk, sk))
+    aligned = torch.empty(s, w, device="cuda")
+    backing = torch.empty(s * w + 1, device="cuda")
+    shifted = backing[1:].view(s, w)  # 4 bytes past a 16-byte boundary
+    assert shifted.data_ptr() % 16 != 0
+    attention.streaming_attention_into(q, k, v, aligned)
+    attention.streaming_attention_into(q, k, v, shifted)
+    torch.cuda.synchronize()
+    assert torch.equal(aligned, shifted)
+    ref = oa.naive_attention(q.cpu(), k.cpu(), v.cpu())
+    assert float((aligned.cpu() - ref).abs().max()) <= 2e-5 * float(ref.abs().max())
+
+
 def test_attention_with_other_key_count(cuda):
     g = torch.Generator().manual_seed(9)
     q, k, v = (torch.randn(n, 32, generator=g) for n in (70, 500, 500))
