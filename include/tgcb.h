@@ -84,7 +84,8 @@ typedef struct tgcb_launch_desc {
   uint64_t counter_bytes;  /* 0: no counters (required > 0 for is_gemm 3) */
 } tgcb_launch_desc;
 
-/* Library version string. */
+/* Library version string, naming the NVRTC version that compiles generated kernels in this
+ * process (the first libnvrtc.so.12 the process loaded). */
 const char* tgcb_version(void);
 
 /* Message of the calling thread's last failure ("" if none). */

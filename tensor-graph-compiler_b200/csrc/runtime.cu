@@ -120,7 +120,23 @@ struct tgcb_plan {
 
 extern "C" {
 
-const char* tgcb_version(void) { return "tgcb 0.1 (sm_100a)"; }
+// The NVRTC that compiles generated kernels is whichever libnvrtc.so.12 the process loaded
+// first (torch's own copy when torch was imported before this library), so the version string
+// names it: the cubin cache is keyed by this string, and a cubin is never reused across NVRTCs.
+const char* tgcb_version(void) {
+  static std::string version;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int major = 0, minor = 0;
+    char buf[96];
+    if (nvrtcVersion(&major, &minor) == NVRTC_SUCCESS)
+      snprintf(buf, sizeof(buf), "tgcb 0.2 (sm_100a, nvrtc %d.%d)", major, minor);
+    else
+      snprintf(buf, sizeof(buf), "tgcb 0.2 (sm_100a, nvrtc unknown)");
+    version = buf;
+  });
+  return version.c_str();
+}
 
 const char* tgcb_last_error(void) { return g_last_error.c_str(); }
 
