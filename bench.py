@@ -64,7 +64,7 @@ def parse_args():
     p.add_argument("--only", action="store_true", help="time the chosen workload alone, without the others under 'workloads'")
     p.add_argument("--sub-steps", type=int, default=0, help="timed steps of each nested workload (default: --steps)")
     p.add_argument("--train-rows", type=int, default=65536, help="global batch of the train workload (profiling uses a small one)")
-    p.add_argument("--train-buckets", choices=["final", "per_gradient"], default="final",
+    p.add_argument("--train-buckets", choices=["final", "per_gradient", "two"], default="final",
                    help="train: one grouped gradient all-reduce after the backward, or one per gradient as it becomes final")
     return p.parse_args()
 
@@ -255,6 +255,48 @@ class NvmlClockSampler:
 # ----------------------------------------------------------------------------- workloads
 
 
+def library_gemm_reference(runner, shapes, steps: int, int8: bool = False) -> dict:
+    """cuBLAS (through torch) on the same GEMM shapes, timed the same way (L2 flushed, events
+    around each call): a like-for-like library reference for the tensor-core kernels, not part
+    of any measured step. TF32 for float32 (torch.mm with TF32 allowed), int8 x int8 -> int32
+    (torch._int_mm) for int8."""
+    import torch
+
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    out = {}
+    try:
+        for name, (m, k, n) in shapes.items():
+            if int8:
+                a = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=runner.device)
+                b = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=runner.device).t()  # [k, n], K-major
+                fn = lambda a=a, b=b: torch._int_mm(a, b)  # noqa: E731
+            else:
+                a = torch.randn(m, k, device=runner.device)
+                b = torch.randn(k, n, device=runner.device)
+                c = torch.empty(m, n, device=runner.device)
+                fn = lambda a=a, b=b, c=c: torch.mm(a, b, out=c)  # noqa: E731
+
+            def step(fn=fn):
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                fn()
+                e.record()
+                e.synchronize()
+                return [s.elapsed_time(e)]
+
+            for _ in range(3):
+                step()
+            ms = runner.timed(step, steps)[0] / steps
+            rate = 2.0 * m * k * n / (ms * 1e-3) / 1e12
+            out[name] = {"shape_mkn": [m, k, n], "us": round(ms * 1e3, 2), ("TOP/s" if int8 else "TFLOP/s"): round(rate, 1)}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    out["what"] = ("cuBLAS through torch (" + ("torch._int_mm, int32 output only" if int8 else "torch.mm, TF32, no epilogue")
+                   + "), same flush and event discipline as the measured steps; a library reference, not a step")
+    return out
+
+
 class GraphWorkload:
     """A workload that is one tgc graph compiled by tgcb.runtime.compile_graph."""
 
@@ -387,6 +429,13 @@ class MlpWorkload(GraphWorkload):
         from tgcb import workloads
 
         return workloads.mlp_inputs(rows=self.rows, seed=self.rank)
+
+    def extras(self, runner, steps: int) -> dict:
+        ref = library_gemm_reference(runner, {"gemm1": (self.rows, 1024, 4096), "gemm2": (self.rows, 4096, 1024)}, steps)
+        if runner.rank != 0:
+            return {}
+        ref["gemm1_plus_gemm2_us"] = round(ref["gemm1"]["us"] + ref["gemm2"]["us"], 2)
+        return {"library_reference": ref}
 
     def config(self):
         return {
@@ -609,6 +658,10 @@ class Int8Workload(GraphWorkload):
 
     def h2d_bytes(self) -> int:
         return self.a_host.numel() * 4
+
+    def extras(self, runner, steps: int) -> dict:
+        ref = library_gemm_reference(runner, {"gemm": (self.rows, self.k, self.n)}, steps, int8=True)
+        return {"library_reference": ref} if runner.rank == 0 else {}
 
     def kernel_work(self) -> list[dict]:
         quant = self.rows * self.k * 4 + self.rows * self.k + self.rows * 4
@@ -1285,9 +1338,11 @@ def measure(name: str, runner: Runner, steps: int, warmup: int, with_cpu: bool) 
         if hasattr(wl, "parallelism"):
             parallelism = wl.parallelism(n)
         elif name == "train":
-            parallelism = f"dp{n}: {wl.global_rows // n} rows per GPU, gradients averaged by NCCL all-reduce " + (
-                "as one grouped call after the backward" if args.train_buckets == "final"
-                else "per gradient, overlapped with the backward")
+            parallelism = f"dp{n}: {wl.global_rows // n} rows per GPU, gradients averaged by NCCL all-reduce " + {
+                "final": "as one grouped call after the backward",
+                "per_gradient": "per gradient, overlapped with the backward",
+                "two": "in two grouped calls: dW2 and db2 beside the last GEMM, dW1 and db1 after it",
+            }[args.train_buckets]
         else:
             parallelism = f"dp{n}: independent row shards per GPU, no collective"
         result = {

@@ -71,8 +71,11 @@ class DataParallelTrainStep:
         """``buckets``: "per_gradient" starts each gradient's all-reduce as soon as the launch that
         finalises it is queued; "final" averages all gradients in one grouped NCCL call after the
         last launch (one collective's latency instead of four; the GEMMs occupy every SM, so
-        collectives queued beside them barely overlap anyway)."""
-        if buckets not in ("per_gradient", "final"):
+        collectives queued beside them barely overlap anyway); "two" averages the gradients that
+        are final before the last GEMM launch in one grouped call started on a side stream as
+        soon as they are (it runs beside the last GEMM, which leaves SMs free when it has fewer
+        output tiles than SM pairs), and the rest in one grouped call at the end."""
+        if buckets not in ("per_gradient", "final", "two"):
             raise ConfigError(f"unknown bucketing {buckets!r}")
         self.buckets = buckets
         self.global_rows = global_rows
@@ -97,6 +100,13 @@ class DataParallelTrainStep:
             outs = list(self.compiled.module.output_names)
             self.finals = sorted({writers[o] for o in outs})
             self.out_at = {k: [i for i, o in enumerate(outs) if writers[o] == k] for k in self.finals}
+            # "two": the launch index of the last GEMM; gradients final before it form the early bucket
+            kinds = [s.kind for s in self.compiled.module.steps for _ in s.launches]
+            last_gemm = max((i for i, k in enumerate(kinds) if k == "gemm"), default=len(kinds))
+            early = [k for k in self.finals if k < last_gemm]
+            self.early_end = (max(early) + 1) if early else 0
+            self.early_outs = [i for k in early for i in self.out_at[k]]
+            self.late_outs = [i for k in self.finals if k >= last_gemm for i in self.out_at[k]]
 
     def shard(self, x, target):
         """This rank's rows of the global batch."""
@@ -144,6 +154,15 @@ class DataParallelTrainStep:
                 e.record(main)
                 timing.append((s, e))
 
+        if self.buckets == "two" and self.early_outs:
+            run(0, self.early_end)
+            done = self.early_end
+            if self.dist is not None and self.world > 1:
+                ev = torch.cuda.Event()
+                ev.record(main)
+                with torch.cuda.stream(self.comm):
+                    self.comm.wait_event(ev)
+                    self._average([outs[i] for i in self.early_outs])
         if self.buckets == "per_gradient":
             for k in self.finals:
                 run(done, k + 1 - done)
@@ -158,6 +177,8 @@ class DataParallelTrainStep:
             run(done, total - done)
         if self.buckets == "final" and self.dist is not None and self.world > 1:
             self._average(list(outs))
+        if self.buckets == "two" and self.dist is not None and self.world > 1:
+            self._average([outs[i] for i in (self.late_outs if self.early_outs else range(len(outs)))])
         if self.dist is not None and self.world > 1:
             main.wait_stream(self.comm)
         return outs

@@ -35,6 +35,26 @@ def test_single_rank_step_matches_oracle(cuda):
         assert rel_err(g, r) < TF32_TOL
 
 
+def test_two_buckets_split_at_the_last_gemm(cuda):
+    """With buckets="two" the gradients final before the last GEMM launch (dW2, db2: the last
+    GEMM computes dW1) form the early bucket; dW1 and db1 the late one. On one rank the step is
+    the plain step."""
+    rows = 512
+    feeds = workloads.mlp_inputs(rows=rows, target=True)
+    step = parallel.DataParallelTrainStep(rows, 1, 0, buckets="two")
+    names = list(step.compiled.module.output_names)
+    assert sorted(step.early_outs + step.late_outs) == list(range(len(names)))
+    assert [names[i] for i in step.early_outs] and [names[i] for i in step.late_outs]
+    kinds = [s.kind for s in step.compiled.module.steps for _ in s.launches]
+    assert kinds[step.early_end - 1] != "gemm" or step.early_end < len(kinds)
+    assert "gemm" in kinds[step.early_end:]  # the last GEMM runs after the early bucket is final
+    grads = step.step({k: v.cuda() for k, v in feeds.items()})
+    torch.cuda.synchronize()
+    ref = interp.run(step.graph, feeds)
+    for g, r in zip(grads, ref, strict=True):
+        assert rel_err(g, r) < TF32_TOL
+
+
 @pytest.mark.parametrize("rows", [8192, 65536])
 def test_full_size_step_matches_oracle(cuda, rows):
     """The training step at the sizes the benchmark runs: one 8192-row shard (8 GPUs) and the
@@ -59,7 +79,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _nccl_rank(rank: int, world: int, port: int, rows: int, out_dir: str) -> None:
+def _nccl_rank(rank: int, world: int, port: int, rows: int, out_dir: str, buckets: str = "final") -> None:
     import datetime
 
     import torch.distributed as dist
@@ -70,7 +90,7 @@ def _nccl_rank(rank: int, world: int, port: int, rows: int, out_dir: str) -> Non
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=datetime.timedelta(seconds=60))
     try:
         feeds = workloads.mlp_inputs(rows=rows, target=True)
-        step = parallel.DataParallelTrainStep(rows, world, rank, dist=dist, device=dev)
+        step = parallel.DataParallelTrainStep(rows, world, rank, dist=dist, device=dev, buckets=buckets)
         x, t = step.shard(feeds["x"], feeds["target"])
         shard = {**{k: feeds[k] for k in parallel.GRADS}, "x": x.contiguous(), "target": t.contiguous()}
         grads = step.step({k: v.to(dev) for k, v in shard.items()})
@@ -82,9 +102,10 @@ def _nccl_rank(rank: int, world: int, port: int, rows: int, out_dir: str) -> Non
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_nccl_ranks_match_the_whole_batch(tmp_path):
+@pytest.mark.parametrize("buckets", ["final", "two", "per_gradient"])
+def test_two_nccl_ranks_match_the_whole_batch(tmp_path, buckets):
     rows, world = 1024, 2
-    mp.start_processes(_nccl_rank, args=(world, _free_port(), rows, str(tmp_path)), nprocs=world, start_method="spawn")
+    mp.start_processes(_nccl_rank, args=(world, _free_port(), rows, str(tmp_path), buckets), nprocs=world, start_method="spawn")
     feeds = workloads.mlp_inputs(rows=rows, target=True)
     ref = interp.run(parallel.train_graph(rows), feeds)
     r0 = torch.load(os.path.join(tmp_path, "rank0.pt"))
