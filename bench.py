@@ -1407,6 +1407,12 @@ def _main(json_out) -> int:
             return 0
         return run_reference(args, n, json_out)
 
+    if world > 1:
+        # communicator set-up lines on stderr (which ranks joined, over which transport); NCCL
+        # reads these once, when torch first loads it, so they are set before torch is imported
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION", "WARN"):
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
     import torch
 
     torch.cuda.set_device(local)
@@ -1417,9 +1423,6 @@ def _main(json_out) -> int:
 
         import torch.distributed as dist_mod
 
-        # communicator set-up lines on stderr: which ranks joined, over which transport
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist_mod.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
         dist = dist_mod
 

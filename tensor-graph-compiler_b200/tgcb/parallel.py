@@ -67,14 +67,16 @@ class DataParallelTrainStep:
     """
 
     def __init__(self, global_rows: int, world: int, rank: int, *, d: int = 1024, f: int = 4096, dist=None,
-                 device=None, executor: Callable | None = None, buckets: str = "final"):
+                 device=None, executor: Callable | None = None, buckets: str = "final", side_ctas: int = 16):
         """``buckets``: "per_gradient" starts each gradient's all-reduce as soon as the launch that
         finalises it is queued; "final" averages all gradients in one grouped NCCL call after the
         last launch (one collective's latency instead of four; the GEMMs occupy every SM, so
         collectives queued beside them barely overlap anyway); "two" averages the gradients that
         are final before the last GEMM launch in one grouped call started on a side stream as
         soon as they are (it runs beside the last GEMM, which leaves SMs free when it has fewer
-        output tiles than SM pairs), and the rest in one grouped call at the end."""
+        output tiles than SM pairs), and the rest in one grouped call at the end. With NCCL the
+        side call runs in its own communicator limited to ``side_ctas`` CTAs, so that it fits in
+        the SMs the last GEMM leaves free instead of delaying that GEMM's resident pairs."""
         if buckets not in ("per_gradient", "final", "two"):
             raise ConfigError(f"unknown bucketing {buckets!r}")
         self.buckets = buckets
@@ -107,23 +109,28 @@ class DataParallelTrainStep:
             self.early_end = (max(early) + 1) if early else 0
             self.early_outs = [i for k in early for i in self.out_at[k]]
             self.late_outs = [i for k in self.finals if k >= last_gemm for i in self.out_at[k]]
+            self.side_group = None
+            if buckets == "two" and dist is not None and world > 1 and dist.get_backend() == "nccl":
+                opts = dist.ProcessGroupNCCL.Options()
+                opts.config.max_ctas = side_ctas
+                self.side_group = dist.new_group(ranks=list(range(world)), backend="nccl", pg_options=opts)
 
     def shard(self, x, target):
         """This rank's rows of the global batch."""
         return x[self.first : self.first + self.rows], target[self.first : self.first + self.rows]
 
-    def _average(self, tensors: list) -> None:
+    def _average(self, tensors: list, group=None) -> None:
         if self.dist is None or self.world == 1:
             return
         if self.dist.get_backend() == "nccl":
             if len(tensors) > 1:
                 from torch.distributed.distributed_c10d import _coalescing_manager
 
-                with _coalescing_manager(device=tensors[0].device):
+                with _coalescing_manager(group=group, device=tensors[0].device):
                     for t in tensors:
-                        self.dist.all_reduce(t, op=self.dist.ReduceOp.AVG)
+                        self.dist.all_reduce(t, op=self.dist.ReduceOp.AVG, group=group)
             else:
-                self.dist.all_reduce(tensors[0], op=self.dist.ReduceOp.AVG)
+                self.dist.all_reduce(tensors[0], op=self.dist.ReduceOp.AVG, group=group)
         else:
             for t in tensors:
                 self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
@@ -162,7 +169,7 @@ class DataParallelTrainStep:
                 ev.record(main)
                 with torch.cuda.stream(self.comm):
                     self.comm.wait_event(ev)
-                    self._average([outs[i] for i in self.early_outs])
+                    self._average([outs[i] for i in self.early_outs], group=self.side_group)
         if self.buckets == "per_gradient":
             for k in self.finals:
                 run(done, k + 1 - done)
