@@ -66,6 +66,8 @@ def parse_args():
     p.add_argument("--train-rows", type=int, default=65536, help="global batch of the train workload (profiling uses a small one)")
     p.add_argument("--train-buckets", choices=["final", "per_gradient", "two"], default="final",
                    help="train: one grouped gradient all-reduce after the backward, or one per gradient as it becomes final")
+    p.add_argument("--train-side-ctas", type=int, default=16,
+                   help="train with two buckets: CTA limit of the communicator that runs the early bucket")
     return p.parse_args()
 
 
@@ -852,6 +854,7 @@ class TrainWorkload:
     machine_kind = "tf32"
     scaling = "strong"
     buckets = "final"
+    side_ctas = 16
     global_rows = 65536
     payload = 2 * 1024 * 4096 * 4 + 4096 * 4 + 1024 * 4
 
@@ -878,7 +881,7 @@ class TrainWorkload:
 
         self.world = world
         self.step_obj = parallel.DataParallelTrainStep(self.global_rows, world, self.rank, dist=dist, device=device,
-                                                       buckets=self.buckets)
+                                                       buckets=self.buckets, side_ctas=self.side_ctas)
         self.g = self.step_obj.graph
         feeds = workloads.mlp_inputs(rows=self.global_rows, target=True)
         x, t = self.step_obj.shard(feeds["x"], feeds["target"])
@@ -1201,6 +1204,7 @@ def make_workload(name: str, runner: Runner):
     if name == "train":
         wl.global_rows = runner.args.train_rows
         wl.buckets = runner.args.train_buckets
+        wl.side_ctas = runner.args.train_side_ctas
         wl.setup(runner.device, runner.dist, runner.n)
     elif name == "longsum":
         wl.setup(runner.device, runner.dist, runner.n)
@@ -1341,7 +1345,7 @@ def measure(name: str, runner: Runner, steps: int, warmup: int, with_cpu: bool) 
             parallelism = f"dp{n}: {wl.global_rows // n} rows per GPU, gradients averaged by NCCL all-reduce " + {
                 "final": "as one grouped call after the backward",
                 "per_gradient": "per gradient, overlapped with the backward",
-                "two": "in two grouped calls: dW2 and db2 beside the last GEMM, dW1 and db1 after it",
+                "two": "in two grouped calls: dW1 and db1 beside the last GEMM (dW2), dW2 and db2 after it",
             }[args.train_buckets]
         else:
             parallelism = f"dp{n}: independent row shards per GPU, no collective"
