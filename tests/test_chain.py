@@ -34,6 +34,30 @@ def test_the_mlp_block_schedule_beats_two_launches():
     assert firsts[0][1] == 0
 
 
+def test_balanced_lists_end_sooner_for_the_mlp_block(monkeypatch):
+    monkeypatch.setattr(chain, "BALANCED", False)
+    greedy, greedy_span = chain.schedule(512, 16, 32, 128, 4, 128, 74)
+    monkeypatch.setattr(chain, "BALANCED", True)
+    lists, span = chain.schedule(512, 16, 32, 128, 4, 128, 74)
+    assert span < greedy_span
+    assert chain.simulate(lists, 512, 16, chain.tile_cost(32), 128, 4, chain.tile_cost(128)) == span
+    # pairs with fewer second-GEMM tiles take more first-GEMM tiles
+    by_second = {}
+    for lst in lists:
+        n2 = sum(1 for t in lst if t >= 512)
+        by_second.setdefault(n2, set()).add(len(lst) - n2)
+    counts = sorted(by_second)
+    assert len(counts) > 1 and min(by_second[counts[0]]) > max(by_second[counts[-1]])
+
+
+def test_every_split_gives_lists_without_wait_cycles():
+    c1, c2 = chain.tile_cost(32), chain.tile_cost(128)
+    for counts in chain._splits(128, 74):
+        assert sum(counts) == 128 and len(counts) == 74
+        lists = chain._balanced(512, c1, 128, c2, counts)
+        chain.check(lists, 512, 16, 128, 4)
+
+
 def test_check_refuses_a_missing_or_repeated_tile():
     with pytest.raises(CodegenError, match="exactly once"):
         chain.check([[0, 1], [3]], 2, 1, 2, 1)  # second-GEMM tile 0 (item 2) missing
