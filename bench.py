@@ -64,7 +64,7 @@ def parse_args():
     p.add_argument("--only", action="store_true", help="time the chosen workload alone, without the others under 'workloads'")
     p.add_argument("--sub-steps", type=int, default=0, help="timed steps of each nested workload (default: --steps)")
     p.add_argument("--train-rows", type=int, default=65536, help="global batch of the train workload (profiling uses a small one)")
-    p.add_argument("--train-buckets", choices=["final", "per_gradient", "two"], default="final",
+    p.add_argument("--train-buckets", choices=["final", "per_gradient", "two", "peer"], default="final",
                    help="train: one grouped gradient all-reduce after the backward, or one per gradient as it becomes final")
     p.add_argument("--train-side-ctas", type=int, default=16,
                    help="train with two buckets: CTA limit of the communicator that runs the early bucket")
@@ -336,7 +336,11 @@ class GraphWorkload:
         self.compiled.check_status()
 
     def launches_per_step(self) -> int:
-        return self.compiled.launches_per_call
+        # the peer all-reduce adds one kernel per bucket
+        extra = 0
+        if self.step_obj.peer is not None:
+            extra = 2 if self.step_obj.early_outs else 1
+        return self.compiled.launches_per_call + extra
 
     def step_profiled(self) -> list[float]:
         return self.compiled.run_profiled(self.arena, self.dev_feeds)[1]
@@ -894,7 +898,11 @@ class TrainWorkload:
         self.compiled = self.step_obj.compiled
 
     def launches_per_step(self) -> int:
-        return self.compiled.launches_per_call
+        # the peer all-reduce adds one kernel per bucket
+        extra = 0
+        if self.step_obj.peer is not None:
+            extra = 2 if self.step_obj.early_outs else 1
+        return self.compiled.launches_per_call + extra
 
     def step_profiled(self) -> list[float]:
         import torch
@@ -910,6 +918,9 @@ class TrainWorkload:
         total = s.elapsed_time(e)
         return per + [max(0.0, total - sum(per))]
 
+    def close(self) -> None:
+        self.step_obj.close()
+
     def step_e2e(self) -> None:
         outs = self.step_obj.step(self.host_feeds)
         for o, h in zip(outs, self.out_host, strict=True):
@@ -923,7 +934,8 @@ class TrainWorkload:
 
     def kernel_work(self) -> list[dict]:
         return GraphWorkload.kernel_work(self) + [
-            {"name": "exposed NCCL all-reduce and gaps", "kind": "allreduce", "bound": "nvlink", "work": self.payload}
+            {"name": "exposed peer all-reduce and gaps" if self.buckets == "peer" else "exposed NCCL all-reduce and gaps",
+             "kind": "allreduce", "bound": "nvlink", "work": self.payload}
         ]
 
     def extras(self, runner, steps: int) -> dict:
@@ -961,6 +973,25 @@ class TrainWorkload:
 
         big_ms = timed_ar(flat, 10)
         tiny_ms = timed_ar(one, 10)
+        peer_ms = None
+        if self.step_obj.peer is not None:
+            # the library's own all-reduce over the same four gradients, in a slot of its own
+            from tgcb.codegen import NUM_SMS
+
+            outs = self.step_obj.step(self.dev_feeds)
+            main = torch.cuda.current_stream()
+            for _ in range(3):
+                self.step_obj.peer.allreduce_avg(outs, 2, main, NUM_SMS)
+            total = 0.0
+            for _ in range(10):
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(main)
+                self.step_obj.peer.allreduce_avg(outs, 2, main, NUM_SMS)
+                e.record(main)
+                e.synchronize()
+                total += s.elapsed_time(e)
+            peer_ms = runner.max_over_ranks(total) / 10
+            self.step_obj.compiled.check_status()
         if runner.rank != 0:
             return {}
         link = collective.nvlink(latency_seconds=tiny_ms * 1e-3 / (2 * (n - 1)))
@@ -979,7 +1010,15 @@ class TrainWorkload:
                 "how": "NCCL AVG over one flat buffer of the gradient set's size; the step itself reduces the four "
                        "gradients in one grouped call after the backward",
             }
-        }
+        } | ({
+            "peer_allreduce": {
+                "bytes": self.payload,
+                "measured_us": round(peer_ms * 1e3, 2),
+                "measured_busbw_gbs": round(collective.bus_bandwidth(self.payload, n, peer_ms * 1e-3) / 1e9, 1),
+                "how": "tgcb_peer_allreduce_avg_f32 over the four gradients in the step's shared arena, one CTA per SM, "
+                       "10 calls after 3 warm-ups, each event-timed, max over ranks",
+            }
+        } if peer_ms is not None else {})
 
     def cpu_program(self):
         """One 8192-row shard of the step by the oracle (the full 65536 rows take minutes on a CPU)."""
@@ -1346,6 +1385,8 @@ def measure(name: str, runner: Runner, steps: int, warmup: int, with_cpu: bool) 
                 "final": "as one grouped call after the backward",
                 "per_gradient": "per gradient, overlapped with the backward",
                 "two": "in two grouped calls: dW1 and db1 beside the last GEMM (dW2), dW2 and db2 after it",
+                "peer": "by tgcb's own all-reduce over NVLink peer memory: dW1 and db1 beside the last GEMM (dW2), "
+                        "dW2 and db2 after it",
             }[args.train_buckets]
         else:
             parallelism = f"dp{n}: independent row shards per GPU, no collective"
@@ -1392,6 +1433,8 @@ def measure(name: str, runner: Runner, steps: int, warmup: int, with_cpu: bool) 
         result.update(extras or {})
         if with_cpu:
             result["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
+    if hasattr(wl, "close"):
+        wl.close()  # collective where the workload shares memory with the other ranks
     del wl
     torch.cuda.synchronize()
     torch.cuda.empty_cache()

@@ -221,6 +221,57 @@ int tgcb_sum_pairwise_f32_noalloc(const float* x, uint64_t n, int block, float* 
  * [-128, 127]. Writes q[rows*cols] (int8) and scale[rows] (float32). */
 int tgcb_quantise_rows_i8(const float* x, int64_t rows, int64_t cols, int8_t* q, float* scale, void* stream);
 
+/* ---- Peer memory and the gradient all-reduce over NVLink (one process per GPU) ----
+ * Replaces what tgc only models: the all-reduce of data-parallel gradients priced by
+ * tgc/parallel/collective.py:76-113 (ring_time, ring_volume) after shard.row_parallel
+ * (tgc/parallel/shard.py:39-123). Buffers are shared between the processes of one box with
+ * CUDA IPC (plain peer mappings over NVLink/NVSwitch; no multicast objects). */
+#define TGCB_MAX_PEERS 8
+#define TGCB_PEER_SLOTS 4
+#define TGCB_PEER_MAX_SEGMENTS 8
+#define TGCB_PEER_HANDLE_BYTES 64
+/* Flag words a peer group needs per rank (ready and done words of every slot). */
+#define TGCB_PEER_FLAG_WORDS (2 * TGCB_PEER_SLOTS * TGCB_MAX_PEERS)
+
+/* cudaMalloc `bytes`, zero them and export them: *ptr is the local address, handle
+ * (TGCB_PEER_HANDLE_BYTES) opens the same memory in another process of the box. */
+int tgcb_peer_alloc(size_t bytes, void** ptr, void* handle);
+/* cudaFree a buffer from tgcb_peer_alloc (NULL: nothing). Close it in every other process first. */
+int tgcb_peer_free(void* ptr);
+/* Map another process's buffer into this one (peer access enabled as needed). */
+int tgcb_peer_open(const void* handle, void** ptr);
+/* Unmap a buffer opened with tgcb_peer_open (NULL: nothing). */
+int tgcb_peer_close(void* ptr);
+
+/* One rank's view of a peer group: every rank's base address (this rank's own, the others'
+ * from tgcb_peer_open) and every rank's flag words (TGCB_PEER_FLAG_WORDS zeroed words each). */
+typedef struct tgcb_peer_group {
+  int32_t rank;
+  int32_t world;                   /* 1 .. TGCB_MAX_PEERS */
+  void* bases[TGCB_MAX_PEERS];     /* 16-byte aligned */
+  uint32_t* flags[TGCB_MAX_PEERS];
+} tgcb_peer_group;
+
+/* float32 values at `offset` bytes (a multiple of 16) from every rank's base, `count` of them
+ * (a positive multiple of 4). */
+typedef struct tgcb_segment {
+  uint64_t offset;
+  uint64_t count;
+} tgcb_segment;
+
+/* Average the segments over the ranks, in place on every rank (what
+ * dist.all_reduce(op=AVG) does, and what tgc's ring_time prices). Every rank calls it with
+ * the same segments, slot, epoch and ctas; the epoch of a slot goes up by one per call,
+ * starting at 1 (flags are never reset; 2^32 / ctas calls per slot). Rank r owns the r-th
+ * share of the 16-byte vectors and, for each of them, adds the ranks' values in rank order
+ * 0, 1, ..., divides by world and stores the result on every rank: the averages are
+ * identical on all ranks and on every run. The kernel (ctas CTAs of 512 threads on `stream`)
+ * ends when this rank's segments hold the averages. Calls in different slots may overlap.
+ * Waits for other ranks are bounded (4 s): a rank that gives up records status 5 in the
+ * device status word (tgcb_status) and returns. */
+int tgcb_peer_allreduce_avg_f32(const tgcb_peer_group* g, const tgcb_segment* segs, int n_segs, int slot,
+                                uint32_t epoch, int ctas, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

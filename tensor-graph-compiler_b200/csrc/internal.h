@@ -15,4 +15,8 @@ int tgcb_internal_fail(int code, const char* what, const char* detail);
 // module on that device (lazy loading), which is when the driver places the array.
 int tgcb_internal_noalloc_setup(int device);
 
+// The current device's status word (initialising the device's state on first use), for
+// kernels launched outside a plan that report device-side failures the way plans do.
+int tgcb_internal_status_word(int** out);
+
 #endif  // TGCB_INTERNAL_H_

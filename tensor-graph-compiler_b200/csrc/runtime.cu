@@ -84,6 +84,14 @@ int current_state(DeviceState** out) {
 
 int tgcb_internal_fail(int code, const char* what, const char* detail) { return fail(code, "%s: %s", what, detail); }
 
+int tgcb_internal_status_word(int** out) {
+  DeviceState* st = nullptr;
+  int rc = current_state(&st);
+  if (rc != TGCB_OK) return rc;
+  *out = st->status;
+  return TGCB_OK;
+}
+
 // A loaded module. Its code is context-independent, so plans may run it on any device and
 // stream. `done` holds, per device and stream it ran on, an event recorded behind the last
 // launches queued there; tgcb_module_unload waits for all of them before releasing the code.

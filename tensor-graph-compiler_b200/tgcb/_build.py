@@ -16,7 +16,7 @@ SOURCE_DIR = os.path.join(os.path.dirname(PACKAGE_DIR), "csrc")
 INCLUDE_DIR = os.path.join(os.path.dirname(os.path.dirname(PACKAGE_DIR)), "include")
 LIBRARY = os.path.join(PACKAGE_DIR, "libtgcb.so")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
-SOURCES = ("runtime.cu", "reductions.cu", "attention.cu")
+SOURCES = ("runtime.cu", "reductions.cu", "attention.cu", "peer.cu")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

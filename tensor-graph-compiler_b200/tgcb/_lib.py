@@ -57,6 +57,28 @@ class LaunchDesc(ctypes.Structure):
 
 
 # Every symbol include/tgcb.h declares, with its ctypes signature.
+MAX_PEERS = 8
+PEER_HANDLE_BYTES = 64
+PEER_FLAG_WORDS = 2 * 4 * MAX_PEERS
+
+
+class PeerGroupDesc(ctypes.Structure):
+    """tgcb_peer_group: one rank's view of every rank's base address and flag words."""
+
+    _fields_ = [
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("bases", ctypes.c_void_p * MAX_PEERS),
+        ("flags", ctypes.c_void_p * MAX_PEERS),
+    ]
+
+
+class Segment(ctypes.Structure):
+    """tgcb_segment: float32 values at a byte offset from every rank's base."""
+
+    _fields_ = [("offset", ctypes.c_uint64), ("count", ctypes.c_uint64)]
+
+
 SIGNATURES = {
     "tgcb_version": (ctypes.c_char_p, []),
     "tgcb_last_error": (ctypes.c_char_p, []),
@@ -113,6 +135,15 @@ SIGNATURES = {
     "tgcb_sum_pairwise_f32_noalloc": (
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p],
+    ),
+    "tgcb_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]),
+    "tgcb_peer_free": (ctypes.c_int, [ctypes.c_void_p]),
+    "tgcb_peer_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "tgcb_peer_close": (ctypes.c_int, [ctypes.c_void_p]),
+    "tgcb_peer_allreduce_avg_f32": (
+        ctypes.c_int,
+        [ctypes.POINTER(PeerGroupDesc), ctypes.POINTER(Segment), ctypes.c_int, ctypes.c_int, ctypes.c_uint32, ctypes.c_int,
+         ctypes.c_void_p],
     ),
     "tgcb_quantise_rows_i8": (
         ctypes.c_int,

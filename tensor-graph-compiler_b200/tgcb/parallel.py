@@ -76,8 +76,13 @@ class DataParallelTrainStep:
         soon as they are (it runs beside the last GEMM, which leaves SMs free when it has fewer
         output tiles than SM pairs), and the rest in one grouped call at the end. With NCCL the
         side call runs in its own communicator limited to ``side_ctas`` CTAs, so that it fits in
-        the SMs the last GEMM leaves free instead of delaying that GEMM's resident pairs."""
-        if buckets not in ("per_gradient", "final", "two"):
+        the SMs the last GEMM leaves free instead of delaying that GEMM's resident pairs.
+        "peer" splits the gradients the same way but averages them with this library's own
+        all-reduce over NVLink peer memory (``tgcb.peer``; the arena is shared with the other
+        ranks of the box): the early bucket in ``side_ctas`` CTAs on a side stream beside the
+        last GEMM, the rest in one CTA per SM after it. Its averages are summed in rank order,
+        identical on every rank and every run."""
+        if buckets not in ("per_gradient", "final", "two", "peer"):
             raise ConfigError(f"unknown bucketing {buckets!r}")
         self.buckets = buckets
         self.global_rows = global_rows
@@ -95,7 +100,14 @@ class DataParallelTrainStep:
             self.torch = torch
             self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
             self.compiled = compile_graph(self.graph, device=self.device.index)
-            self.arena = self.compiled.new_arena()
+            self.peer = None
+            if buckets == "peer" and dist is not None and world > 1:
+                from tgcb.peer import PeerGroup
+
+                self.peer = PeerGroup(dist, self.compiled.arena_bytes, self.device.index)
+                self.arena = self.peer.buffer
+            else:
+                self.arena = self.compiled.new_arena()
             self.comm = torch.cuda.Stream(device=self.device)
             # where each gradient becomes final: split the plan there
             writers = self.compiled.launch_writers()
@@ -110,6 +122,7 @@ class DataParallelTrainStep:
             self.early_outs = [i for k in early for i in self.out_at[k]]
             self.late_outs = [i for k in self.finals if k >= last_gemm for i in self.out_at[k]]
             self.side_group = None
+            self.side_ctas = side_ctas
             if buckets == "two" and dist is not None and world > 1 and dist.get_backend() == "nccl":
                 opts = dist.ProcessGroupNCCL.Options()
                 opts.config.max_ctas = side_ctas
@@ -161,6 +174,8 @@ class DataParallelTrainStep:
                 e.record(main)
                 timing.append((s, e))
 
+        if self.peer is not None:
+            return self._peer_step(run, outs, main)
         if self.buckets == "two" and self.early_outs:
             run(0, self.early_end)
             done = self.early_end
@@ -189,3 +204,30 @@ class DataParallelTrainStep:
         if self.dist is not None and self.world > 1:
             main.wait_stream(self.comm)
         return outs
+
+    def _peer_step(self, run, outs: list, main) -> list:
+        from tgcb.codegen import NUM_SMS
+
+        torch = self.torch
+        total = self.compiled.launches_per_call
+        done = 0
+        if self.early_outs:
+            run(0, self.early_end)
+            done = self.early_end
+            ev = torch.cuda.Event()
+            ev.record(main)
+            self.comm.wait_event(ev)
+            self.peer.allreduce_avg([outs[i] for i in self.early_outs], 0, self.comm, self.side_ctas)
+        if done < total:
+            run(done, total - done)
+        late = self.late_outs if self.early_outs else list(range(len(outs)))
+        self.peer.allreduce_avg([outs[i] for i in late], 1, main, NUM_SMS)
+        main.wait_stream(self.comm)
+        return outs
+
+    def close(self) -> None:
+        """Release the peer buffers (collective: every rank calls it); the gradients returned by
+        ``step`` are views of them and are invalid afterwards."""
+        if getattr(self, "peer", None) is not None:
+            self.peer.close()
+            self.peer = None

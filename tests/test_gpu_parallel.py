@@ -36,8 +36,8 @@ def test_single_rank_step_matches_oracle(cuda):
 
 
 def test_two_buckets_split_at_the_last_gemm(cuda):
-    """With buckets="two" the gradients final before the last GEMM launch (dW2, db2: the last
-    GEMM computes dW1) form the early bucket; dW1 and db1 the late one. On one rank the step is
+    """With buckets="two" the gradients final before the last GEMM launch (dW1, db1: the last
+    GEMM computes dW2) form the early bucket; dW2 and db2 the late one. On one rank the step is
     the plain step."""
     rows = 512
     feeds = workloads.mlp_inputs(rows=rows, target=True)
@@ -112,6 +112,58 @@ def test_two_nccl_ranks_match_the_whole_batch(tmp_path, buckets):
     r1 = torch.load(os.path.join(tmp_path, "rank1.pt"))
     for a, b, r in zip(r0, r1, ref, strict=True):
         assert torch.equal(a, b)
+        assert rel_err(a, r) < TF32_TOL
+
+
+def _peer_rank(rank: int, world: int, port: int, rows: int, out_dir: str) -> None:
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "NCCL_NVLS_ENABLE": "0"})
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=datetime.timedelta(seconds=60))
+    try:
+        feeds = workloads.mlp_inputs(rows=rows, target=True)
+        peer_step = parallel.DataParallelTrainStep(rows, world, rank, dist=dist, device=dev, buckets="peer")
+        nccl_step = parallel.DataParallelTrainStep(rows, world, rank, dist=dist, device=dev, buckets="final")
+        x, t = peer_step.shard(feeds["x"], feeds["target"])
+        shard = {k: v.to(dev) for k, v in {**{k: feeds[k] for k in parallel.GRADS}, "x": x.contiguous(),
+                                           "target": t.contiguous()}.items()}
+        runs = []
+        for _ in range(3):  # three steps: the flags' epochs advance, nothing is reset
+            runs.append([g.clone() for g in peer_step.step(shard)])
+        torch.cuda.synchronize()
+        peer_step.compiled.check_status()
+        ref = nccl_step.step(shard)
+        torch.cuda.synchronize()
+        torch.save({"peer": [[g.cpu() for g in r] for r in runs], "nccl": [g.cpu() for g in ref]},
+                   os.path.join(out_dir, f"peer{rank}.pt"))
+        peer_step.close()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_peer_allreduce_matches_nccl(tmp_path):
+    """buckets="peer": the library's own all-reduce over NVLink peer memory. With two ranks the
+    rank-order sum a + b and NCCL's are the same additions, and the average of two is exact
+    scaling, so the gradients equal NCCL's bit for bit; they are the same on both ranks and
+    on every step, and match the whole-batch oracle."""
+    rows, world = 1024, 2
+    mp.start_processes(_peer_rank, args=(world, _free_port(), rows, str(tmp_path)), nprocs=world, start_method="spawn")
+    feeds = workloads.mlp_inputs(rows=rows, target=True)
+    ref = interp.run(parallel.train_graph(rows), feeds)
+    got = [torch.load(os.path.join(tmp_path, f"peer{r}.pt")) for r in range(world)]
+    for r in range(world):
+        for run in got[r]["peer"]:
+            for a, b in zip(run, got[0]["peer"][0], strict=True):
+                assert torch.equal(a, b)
+        for a, b in zip(got[r]["peer"][0], got[r]["nccl"], strict=True):
+            assert torch.equal(a, b)
+    for a, r in zip(got[0]["peer"][0], ref, strict=True):
         assert rel_err(a, r) < TF32_TOL
 
 
