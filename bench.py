@@ -64,9 +64,9 @@ def parse_args():
     p.add_argument("--only", action="store_true", help="time the chosen workload alone, without the others under 'workloads'")
     p.add_argument("--sub-steps", type=int, default=0, help="timed steps of each nested workload (default: --steps)")
     p.add_argument("--train-rows", type=int, default=65536, help="global batch of the train workload (profiling uses a small one)")
-    p.add_argument("--train-buckets", choices=["final", "per_gradient", "two", "peer"], default="final",
+    p.add_argument("--train-buckets", choices=["final", "per_gradient", "two", "peer"], default="peer",
                    help="train: one grouped gradient all-reduce after the backward, or one per gradient as it becomes final")
-    p.add_argument("--train-side-ctas", type=int, default=16,
+    p.add_argument("--train-side-ctas", type=int, default=20,
                    help="train with two buckets: CTA limit of the communicator that runs the early bucket")
     return p.parse_args()
 
@@ -857,8 +857,8 @@ class TrainWorkload:
     dtype = "tf32"
     machine_kind = "tf32"
     scaling = "strong"
-    buckets = "final"
-    side_ctas = 16
+    buckets = "peer"
+    side_ctas = 20
     global_rows = 65536
     payload = 2 * 1024 * 4096 * 4 + 4096 * 4 + 1024 * 4
 

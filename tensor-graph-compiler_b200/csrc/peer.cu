@@ -110,34 +110,57 @@ __device__ __forceinline__ unsigned long long vector_address(const PeerParams& p
   return 0;  // not reached: i < seg_end[nseg - 1]
 }
 
-template <int WORLD>
-__device__ __forceinline__ void reduce_vector(const PeerParams& p, unsigned long long e) {
-  float4 v[WORLD];
+// U vectors per thread at a time, their WORLD x U loads issued before any addition, so that
+// about eight 16-byte loads per thread are in flight whatever the number of ranks (remote
+// loads are latency-bound over NVLink).
+template <int WORLD, int U>
+__device__ __forceinline__ void reduce_vectors(const PeerParams& p, const unsigned long long (&e)[U], int n) {
+  float4 v[U][WORLD];
 #pragma unroll
-  for (int r = 0; r < WORLD; ++r) v[r] = r == p.rank ? p.base[r][e] : ld_volatile4(p.base[r] + e);
-  float4 acc = v[0];
+  for (int u = 0; u < U; ++u) {
+    if (u < n) {
 #pragma unroll
-  for (int r = 1; r < WORLD; ++r) {
-    acc.x = __fadd_rn(acc.x, v[r].x);
-    acc.y = __fadd_rn(acc.y, v[r].y);
-    acc.z = __fadd_rn(acc.z, v[r].z);
-    acc.w = __fadd_rn(acc.w, v[r].w);
+      for (int r = 0; r < WORLD; ++r) v[u][r] = r == p.rank ? p.base[r][e[u]] : ld_volatile4(p.base[r] + e[u]);
+    }
   }
-  const float n = (float)WORLD;
-  acc = make_float4(__fdiv_rn(acc.x, n), __fdiv_rn(acc.y, n), __fdiv_rn(acc.z, n), __fdiv_rn(acc.w, n));
+  const float w = (float)WORLD;
 #pragma unroll
-  for (int r = 0; r < WORLD; ++r) p.base[r][e] = acc;
+  for (int u = 0; u < U; ++u) {
+    if (u < n) {
+      float4 acc = v[u][0];
+#pragma unroll
+      for (int r = 1; r < WORLD; ++r) {
+        acc.x = __fadd_rn(acc.x, v[u][r].x);
+        acc.y = __fadd_rn(acc.y, v[u][r].y);
+        acc.z = __fadd_rn(acc.z, v[u][r].z);
+        acc.w = __fadd_rn(acc.w, v[u][r].w);
+      }
+      acc = make_float4(__fdiv_rn(acc.x, w), __fdiv_rn(acc.y, w), __fdiv_rn(acc.z, w), __fdiv_rn(acc.w, w));
+#pragma unroll
+      for (int r = 0; r < WORLD; ++r) p.base[r][e[u]] = acc;
+    }
+  }
 }
 
 template <int WORLD>
 __device__ void reduce_share(const PeerParams& p) {
+  constexpr int U = WORLD >= 8 ? 1 : 8 / WORLD;
   const unsigned long long total = p.seg_end[p.nseg - 1];
   const unsigned long long share = (total + WORLD - 1) / WORLD;
   const unsigned long long lo = (unsigned long long)p.rank * share;
   const unsigned long long hi = lo + share < total ? lo + share : total;
   const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
-  for (unsigned long long i = lo + (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < hi; i += stride)
-    reduce_vector<WORLD>(p, vector_address(p, i));
+  for (unsigned long long i = lo + (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < hi; i += U * stride) {
+    unsigned long long e[U];
+    int n = 0;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const unsigned long long k = i + u * stride;
+      e[u] = k < hi ? vector_address(p, k) : 0;
+      n += k < hi ? 1 : 0;
+    }
+    reduce_vectors<WORLD, U>(p, e, n);
+  }
 }
 
 __global__ void __launch_bounds__(kThreads) allreduce_avg(const PeerParams p) {

@@ -7,13 +7,15 @@ tgc/parallel/collective.py prices the gradient all-reduce with a ring model and 
 with the backward pass (collective.py:76-113, 339-379). Here each rank is one process driving
 one GPU; it compiles the gradient graph of its own shard (``tgcb.grad.gradient`` of the MLP's
 mean-squared error over shard_rows rows, lowered by ``tgcb.runtime``), runs it, and averages
-the four gradients over ranks with NCCL over NVLink (``torch.distributed``; AVG, since every
-shard's loss is a mean over the same number of rows, so the global gradient is the mean of the
-shard gradients). By default the four all-reduces are one grouped NCCL call after the last
-launch (``buckets="final"``): the persistent GEMMs hold every SM, so a collective queued beside
-them waits for a gap anyway, and one call pays NCCL's latency once. With
-``buckets="per_gradient"`` each gradient's all-reduce starts on a side stream as soon as the
-launch that finalises it has been queued, overlapping the launches that remain.
+the four gradients over ranks (AVG, since every shard's loss is a mean over the same number
+of rows, so the global gradient is the mean of the shard gradients). By default
+(``buckets="peer"``) they are averaged by this library's own all-reduce over NVLink peer
+memory (``tgcb.peer``): the step's arena is shared with the other ranks of the box, the
+gradients final before the last GEMM (dW1, db1) are averaged by a kernel of ``side_ctas`` CTAs
+on a side stream in the SMs that GEMM leaves free, and the rest (dW2, db2) by one CTA per SM
+after it. The NCCL modes (``torch.distributed``) stay for comparison: ``"final"`` (one grouped
+call after the last launch), ``"per_gradient"`` (each gradient's all-reduce on a side stream
+as soon as the launch that finalises it is queued) and ``"two"`` (the peer mode's split).
 
 The same code runs with the ``gloo`` backend on CPU ranks when ``executor`` replaces the GPU
 plan (tests use the oracle there), which is how the host-side sharding and averaging logic is
@@ -67,7 +69,7 @@ class DataParallelTrainStep:
     """
 
     def __init__(self, global_rows: int, world: int, rank: int, *, d: int = 1024, f: int = 4096, dist=None,
-                 device=None, executor: Callable | None = None, buckets: str = "final", side_ctas: int = 16):
+                 device=None, executor: Callable | None = None, buckets: str = "peer", side_ctas: int = 20):
         """``buckets``: "per_gradient" starts each gradient's all-reduce as soon as the launch that
         finalises it is queued; "final" averages all gradients in one grouped NCCL call after the
         last launch (one collective's latency instead of four; the GEMMs occupy every SM, so
