@@ -336,11 +336,7 @@ class GraphWorkload:
         self.compiled.check_status()
 
     def launches_per_step(self) -> int:
-        # the peer all-reduce adds one kernel per bucket
-        extra = 0
-        if self.step_obj.peer is not None:
-            extra = 2 if self.step_obj.early_outs else 1
-        return self.compiled.launches_per_call + extra
+        return self.compiled.launches_per_call
 
     def step_profiled(self) -> list[float]:
         return self.compiled.run_profiled(self.arena, self.dev_feeds)[1]
@@ -934,7 +930,8 @@ class TrainWorkload:
 
     def kernel_work(self) -> list[dict]:
         return GraphWorkload.kernel_work(self) + [
-            {"name": "exposed peer all-reduce and gaps" if self.buckets == "peer" else "exposed NCCL all-reduce and gaps",
+            {"name": "gaps between launches" if self.world == 1 else
+             "exposed peer all-reduce and gaps" if self.buckets == "peer" else "exposed NCCL all-reduce and gaps",
              "kind": "allreduce", "bound": "nvlink", "work": self.payload}
         ]
 

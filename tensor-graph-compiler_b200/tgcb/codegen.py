@@ -417,6 +417,8 @@ class Lowering:
                 elif kind == "row" and (rs == obj.src_sizes or rs in self._row_shapes(obj.src_sizes)):
                     if self._final_phase_ok(obj, r):
                         owner = latest
+                elif kind == "red" and self._col_epilogue_ok(obj, r, deps):
+                    owner = latest
             if owner is None:
                 maps.setdefault(latest, []).append(r)
             else:
@@ -468,7 +470,7 @@ class Lowering:
             elif kind == "row":
                 new = [self._row_step(item[1], item[2])]
             else:
-                new = self._reduction_steps(item[1])
+                new = self._reduction_steps(item[1], item[2])
             for st in new:
                 st.reads = sorted(set(st.reads) | self._step_reads)
             steps.extend(new)
@@ -885,10 +887,12 @@ class Lowering:
             step.row_body = RowBody("\n".join(lines), nred, R, C)
         return step
 
-    def _reduction_steps(self, node) -> list[Step]:
+    def _reduction_steps(self, node, owned: list[str] | None = None) -> list[Step]:
         kind = self.reduction_kind(node)
         if kind == "col":
-            return self._col_steps(node)
+            return self._col_steps(node, owned or [])
+        if owned:
+            raise CodegenError("only column reductions take requests")
         if kind == "full":
             return self._full_steps(node)
         return [self._naive_step(node)]
@@ -903,8 +907,40 @@ class Lowering:
             return "-INFINITY" if t in ("float", "double") else "(-2147483647-1)"
         return f"({t})0"
 
-    def _col_steps(self, node) -> list[Step]:
-        """Reduction over axis 0 of [R, C]: P row partitions summed sequentially, then the P partials in order."""
+    def _col_epilogue_ok(self, node, r: str, deps) -> bool:
+        """Whether request ``r`` can be computed where a column reduction's final values are: it
+        depends on nothing but that reduction's result, element for element (a reshape or an
+        elementwise function of it, same element count)."""
+        if self.reduction_kind(node) != "col" or set(deps) != {node.name}:
+            return False
+        if _prod(self.sizes(r)) != _prod(self.sizes(node.name)):
+            return False
+        try:
+            self._col_request_lines(node, r, "v")
+        except CodegenError:
+            return False
+        return True
+
+    def _col_request_lines(self, node, r: str, fin: str) -> list[str]:
+        """Statements that store request ``r`` at column c from the reduction's value ``fin``."""
+        red_sizes = self.sizes(node.name)
+
+        def resolve(name, idx):
+            if name != node.name:
+                return None
+            if tuple(i for i, n in zip(idx, red_sizes, strict=True) if n != 1) != ("c",):
+                raise CodegenError("not aligned with the reduction's columns")
+            return fin
+
+        eb = ExprBuilder(self.values, self.producers, lambda n: None, resolve, indent="  ")
+        v = eb.value(r, tuple(delinearise("c", self.sizes(r))))
+        t = ctype(self.values[r].dtype)
+        return eb.lines + [f"  reinterpret_cast<{t}*>({PTR(r)})[c] = {v};"]
+
+    def _col_steps(self, node, owned: list[str] | None = None) -> list[Step]:
+        """Reduction over axis 0 of [R, C]: P row partitions summed sequentially, then the P
+        partials in order. Requests owned by the step (element-wise functions or reshapes of the
+        result, such as a bias gradient's reshape) are stored by the final kernel too."""
         name = node.name
         src = node.inputs[0]
         R, C = self.sizes(src)
@@ -943,7 +979,10 @@ class Lowering:
             f"  const {t}* part = reinterpret_cast<const {t}*>({PTR(scratch)});\n"
             f"  {t} acc = {self._init(opn, t)};\n"
             f"  for (int p = 0; p < {P}; ++p) {{ const {t} v = part[p * {C}LL + c]; {self._acc_update(opn, 'acc', 'v', t)} }}\n"
-            f"  reinterpret_cast<{t}*>({PTR(name)})[c] = {fin};\n}}\n"
+            f"  const {t} fin = {fin};\n"
+            f"  reinterpret_cast<{t}*>({PTR(name)})[c] = fin;\n"
+            + "".join(line + "\n" for r in owned for line in self._col_request_lines(node, r, "fin"))
+            + "}\n"
         )
         reads: list[str] = []  # recorded by _pointer_of while generating
         self.materialised.add(name)
@@ -952,14 +991,14 @@ class Lowering:
                 "colreduce",
                 name,
                 reads=reads,
-                writes=[scratch, name],
+                writes=[scratch, name] + list(owned),
                 source=s1 + "\n" + s2,
                 launches=[
                     Launch(k1, (cblocks, P, 1), (256, 1, 1)),
                     Launch(k2, (cblocks, 1, 1), (256, 1, 1)),
                 ],
                 bracketing=f"partitioned: {P} row blocks of {L} summed sequentially, then the {P} partials in order",
-                nodes=[name],
+                nodes=[name] + list(owned),
             )
         ]
 

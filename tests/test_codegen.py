@@ -250,3 +250,25 @@ def test_chunked_operand_maps_agree_with_the_kernels(ta, tb, M, N, K, kind):
         assert (op.chunks > 0) == kernel_chunked
         if kernel_chunked:
             assert op.cols == extent and op.swizzle == 1 and op.chunks == tile // 32
+
+
+def test_column_reductions_store_their_reshaped_results_themselves():
+    """A request that is the column sum element for element (the bias gradients' reshapes)
+    is stored by the reduction's final kernel: no copy kernel follows it."""
+    from tgcb import parallel
+
+    mod = runtime.generate(parallel.train_graph(512))[3]
+    kinds = [s.kind for s in mod.steps]
+    assert "map" not in kinds and kinds.count("colreduce") == 2
+    for s in mod.steps:
+        if s.kind == "colreduce":
+            assert len(s.writes) == 3 and len(s.launches) == 2
+
+
+def test_requests_not_aligned_with_the_columns_keep_their_own_kernel():
+    b = ir.Builder()
+    x = b.input((4096, 1024), ir.FLOAT32, "x")
+    total = b.sum(x, [0, 1])
+    cols = b.sum(x, [0])
+    mod = runtime.generate(b.finish(total, b.reshape(cols, (32, 32))))[3]
+    assert [s.kind for s in mod.steps] == ["fullreduce", "colreduce", "map"]
