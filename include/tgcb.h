@@ -230,8 +230,9 @@ int tgcb_quantise_rows_i8(const float* x, int64_t rows, int64_t cols, int8_t* q,
 #define TGCB_PEER_SLOTS 4
 #define TGCB_PEER_MAX_SEGMENTS 8
 #define TGCB_PEER_HANDLE_BYTES 64
-/* Flag words a peer group needs per rank (ready and done words of every slot). */
-#define TGCB_PEER_FLAG_WORDS (2 * TGCB_PEER_SLOTS * TGCB_MAX_PEERS)
+/* Flag words a peer group needs per rank (ready and done words of every slot and rank, and a
+ * finished count per slot). */
+#define TGCB_PEER_FLAG_WORDS (2 * TGCB_PEER_SLOTS * TGCB_MAX_PEERS + TGCB_PEER_SLOTS)
 
 /* cudaMalloc `bytes`, zero them and export them: *ptr is the local address, handle
  * (TGCB_PEER_HANDLE_BYTES) opens the same memory in another process of the box. */

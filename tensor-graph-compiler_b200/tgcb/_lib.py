@@ -59,7 +59,7 @@ class LaunchDesc(ctypes.Structure):
 # Every symbol include/tgcb.h declares, with its ctypes signature.
 MAX_PEERS = 8
 PEER_HANDLE_BYTES = 64
-PEER_FLAG_WORDS = 2 * 4 * MAX_PEERS
+PEER_FLAG_WORDS = 2 * 4 * MAX_PEERS + 4
 
 
 class PeerGroupDesc(ctypes.Structure):

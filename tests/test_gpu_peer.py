@@ -58,9 +58,9 @@ def test_one_rank_group_keeps_its_values(cuda):
             torch.cuda.synchronize()
             assert _status() == 0
             assert torch.equal(x, before)
-        # the done counter of slot 0 holds epochs x CTAs, the ready word the last epoch
+        # slot 0's ready and done words hold the last epoch, its finished count epochs x CTAs
         f = _view(flags, _lib.PEER_FLAG_WORDS).view(torch.int32).cpu()
-        assert int(f[0]) == 2 and int(f[4 * _lib.MAX_PEERS]) == 2 * 8
+        assert int(f[0]) == 2 and int(f[4 * _lib.MAX_PEERS]) == 2 and int(f[8 * _lib.MAX_PEERS]) == 2 * 8
     finally:
         torch.cuda.synchronize()
         lib.tgcb_peer_free(ctypes.c_void_p(base))

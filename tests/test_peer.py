@@ -53,5 +53,6 @@ def test_the_c_abi_structures_match_the_header():
     header = open(os.path.join(os.path.dirname(__file__), "..", "include", "tgcb.h")).read()
     assert f"#define TGCB_MAX_PEERS {_lib.MAX_PEERS}" in header
     assert f"#define TGCB_PEER_HANDLE_BYTES {_lib.PEER_HANDLE_BYTES}" in header
-    assert "#define TGCB_PEER_FLAG_WORDS (2 * TGCB_PEER_SLOTS * TGCB_MAX_PEERS)" in header
+    assert "#define TGCB_PEER_FLAG_WORDS (2 * TGCB_PEER_SLOTS * TGCB_MAX_PEERS + TGCB_PEER_SLOTS)" in header
+    assert _lib.PEER_FLAG_WORDS == 2 * 4 * _lib.MAX_PEERS + 4
     assert "#define TGCB_PEER_SLOTS 4" in header and peer.SLOTS == 4
