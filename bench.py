@@ -864,7 +864,7 @@ class TrainWorkload:
     def config(self):
         return {
             "workload": "MLP block training step: d/dW of mean((mlp(x)-target)^2), x,target [65536,1024] batch-sharded, "
-            "W1 [1024,4096], W2 [4096,1024]; gradients averaged by NCCL all-reduce",
+            "W1 [1024,4096], W2 [4096,1024]; gradients averaged over the GPUs by an all-reduce",
             "global_rows": self.global_rows,
             "flops_per_step": 5 * 2 * self.global_rows * 1024 * 4096,
             "allreduce_bytes": self.payload,
@@ -1378,10 +1378,10 @@ def measure(name: str, runner: Runner, steps: int, warmup: int, with_cpu: bool) 
         if hasattr(wl, "parallelism"):
             parallelism = wl.parallelism(n)
         elif name == "train":
-            parallelism = f"dp{n}: {wl.global_rows // n} rows per GPU, gradients averaged by NCCL all-reduce " + {
-                "final": "as one grouped call after the backward",
-                "per_gradient": "per gradient, overlapped with the backward",
-                "two": "in two grouped calls: dW1 and db1 beside the last GEMM (dW2), dW2 and db2 after it",
+            parallelism = f"dp{n}: {wl.global_rows // n} rows per GPU" if n == 1 else f"dp{n}: {wl.global_rows // n} rows per GPU, gradients averaged " + {
+                "final": "by NCCL in one grouped call after the backward",
+                "per_gradient": "by NCCL per gradient, overlapped with the backward",
+                "two": "by NCCL in two grouped calls: dW1 and db1 beside the last GEMM (dW2), dW2 and db2 after it",
                 "peer": "by tgcb's own all-reduce over NVLink peer memory: dW1 and db1 beside the last GEMM (dW2), "
                         "dW2 and db2 after it",
             }[args.train_buckets]
