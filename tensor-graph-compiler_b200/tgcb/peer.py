@@ -46,6 +46,9 @@ def segments_of(tensors, base: int, nbytes: int) -> list[tuple[int, int]]:
         segs.append((off, t.numel()))
     if not 1 <= len(segs) <= 8:
         raise ConfigError("peer all-reduce takes 1 to 8 tensors per call")
+    spans = sorted((o, o + 4 * c) for o, c in segs)
+    if any(a[1] > b[0] for a, b in zip(spans, spans[1:])):
+        raise ConfigError("tensors to all-reduce in one call must not overlap (each element would be averaged twice)")
     return segs
 
 

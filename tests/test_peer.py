@@ -39,6 +39,8 @@ def test_segments_refuse_what_the_kernel_cannot_take():
         peer.segments_of([torch.zeros(8)], base, n)
     with pytest.raises(ConfigError, match="float32"):
         peer.segments_of([buf.view(torch.int32)[0:8]], base, n)
+    with pytest.raises(ConfigError, match="overlap"):
+        peer.segments_of([buf[0:8], buf[4:12]], base, n)
     with pytest.raises(ConfigError, match="1 to 8"):
         peer.segments_of([buf[4 * i : 4 * i + 4] for i in range(9)], base, n)
 
