@@ -251,6 +251,7 @@ typedef struct tgcb_peer_group {
   int32_t world;                   /* 1 .. TGCB_MAX_PEERS */
   void* bases[TGCB_MAX_PEERS];     /* 16-byte aligned */
   uint32_t* flags[TGCB_MAX_PEERS];
+  uint64_t bytes;                  /* size of every rank's buffer at bases[r]: segments must lie inside */
 } tgcb_peer_group;
 
 /* float32 values at `offset` bytes (a multiple of 16) from every rank's base, `count` of them

@@ -271,6 +271,8 @@ int tgcb_peer_allreduce_avg_f32(const tgcb_peer_group* g, const tgcb_segment* se
     if (segs[s].offset % 16 != 0 || segs[s].count % 4 != 0 || segs[s].count == 0)
       return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_peer_allreduce_avg_f32",
                                 "segments start on 16 bytes and hold a positive multiple of 4 floats");
+    if (segs[s].offset > g->bytes || segs[s].count > (g->bytes - segs[s].offset) / 4)
+      return tgcb_internal_fail(TGCB_E_INVALID, "tgcb_peer_allreduce_avg_f32", "a segment reaches past the peer buffers");
     p.seg_off[s] = segs[s].offset / 16;
     end += segs[s].count / 4;
     p.seg_end[s] = end;

@@ -70,6 +70,7 @@ class PeerGroupDesc(ctypes.Structure):
         ("world", ctypes.c_int32),
         ("bases", ctypes.c_void_p * MAX_PEERS),
         ("flags", ctypes.c_void_p * MAX_PEERS),
+        ("bytes", ctypes.c_uint64),
     ]
 
 

@@ -89,7 +89,7 @@ class PeerGroup:
             gathered = [None] * self.world
             dist.all_gather_object(gathered, tuple(handles), group=group)
             desc = _lib.PeerGroupDesc()
-            desc.rank, desc.world = self.rank, self.world
+            desc.rank, desc.world, desc.bytes = self.rank, self.world, nbytes
             for r, (hb, hf) in enumerate(gathered):
                 if r == self.rank:
                     desc.bases[r], desc.flags[r] = self._own

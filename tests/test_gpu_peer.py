@@ -51,7 +51,7 @@ def test_one_rank_group_keeps_its_values(cuda):
         x.copy_(torch.randn(n, generator=torch.Generator().manual_seed(3)).cuda())
         before = x.clone()
         desc = _lib.PeerGroupDesc()
-        desc.rank, desc.world = 0, 1
+        desc.rank, desc.world, desc.bytes = 0, 1, n * 4
         desc.bases[0], desc.flags[0] = base, flags
         for epoch in (1, 2):  # flags are monotonic: a second call needs no reset
             _lib.check(_run(desc, [(0, 4096), (16 * 4096, n - 4 * 4096)], 0, epoch), "all-reduce")
@@ -76,7 +76,7 @@ def test_a_rank_that_never_arrives_times_out_with_a_status(cuda):
     try:
         assert _status() == 0
         desc = _lib.PeerGroupDesc()
-        desc.rank, desc.world = 0, 2
+        desc.rank, desc.world, desc.bytes = 0, 2, n * 4
         desc.bases[0], desc.flags[0] = base, flags
         desc.bases[1], desc.flags[1] = other, other_flags  # nothing runs as rank 1
         _lib.check(_run(desc, [(0, n)], 3, 1, ctas=2), "all-reduce")
@@ -101,6 +101,8 @@ def test_bad_arguments_are_refused_before_any_launch(cuda):
     base, flags = _alloc(64), _alloc(_lib.PEER_FLAG_WORDS * 4)
     try:
         desc.bases[0], desc.flags[0] = base, flags
+        desc.bytes = 64
+        assert _run(desc, [(48, 8)], 0, 1) == _lib.TGCB_E_INVALID  # past the buffer
         assert _run(desc, [(4, 4)], 0, 1) == _lib.TGCB_E_INVALID  # offset not on 16 bytes
         assert _run(desc, [(0, 6)], 0, 1) == _lib.TGCB_E_INVALID  # not a multiple of 4
         assert _run(desc, [(0, 4)], 4, 1) == _lib.TGCB_E_INVALID  # slot

@@ -48,7 +48,7 @@ def test_segments_refuse_what_the_kernel_cannot_take():
 def test_the_c_abi_structures_match_the_header():
     import ctypes
 
-    assert ctypes.sizeof(_lib.PeerGroupDesc) == 8 + 2 * 8 * _lib.MAX_PEERS
+    assert ctypes.sizeof(_lib.PeerGroupDesc) == 8 + 2 * 8 * _lib.MAX_PEERS + 8
     assert ctypes.sizeof(_lib.Segment) == 16
     import os
 
