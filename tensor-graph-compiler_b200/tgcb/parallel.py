@@ -83,7 +83,9 @@ class DataParallelTrainStep:
         all-reduce over NVLink peer memory (``tgcb.peer``; the arena is shared with the other
         ranks of the box): the early bucket in ``side_ctas`` CTAs on a side stream beside the
         last GEMM, the rest in one CTA per SM after it. Its averages are summed in rank order,
-        identical on every rank and every run."""
+        identical on every rank and every run. The default ``side_ctas`` (20) is what the MLP's
+        last GEMM (dW2: 64 pair tiles on 74 SM pairs) leaves free of the 148 SMs; on one 8-GPU
+        box 20 gave 1298 steps/s and 16 gave 1277."""
         if buckets not in ("per_gradient", "final", "two", "peer"):
             raise ConfigError(f"unknown bucketing {buckets!r}")
         self.buckets = buckets
